@@ -1,0 +1,166 @@
+"""Build step for the native libraries (in-tree, sm_100a only).
+
+Produces, under ``inference_performance_lab/_native/``:
+
+* ``libipl_b200.so`` - every CUDA kernel and the C ABI of ``include/ipl_b200.h`` (nvcc, static
+  cudart, no torch dependency);
+* ``inference_performance_lab_cuda.so`` - the stable-LibTorch-ABI op registration
+  (``csrc/torch_ops.cpp``, g++), linked against ``libipl_b200.so`` through ``$ORIGIN``.
+
+Run ``python inference-performance-lab_b200/build.py`` (or call :func:`build`). Rebuilds only what
+is older than its sources or was built with different flags.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PACKAGE_ROOT = Path(__file__).resolve().parent
+REPO_ROOT = PACKAGE_ROOT.parent
+CSRC = PACKAGE_ROOT / "csrc"
+INCLUDE = REPO_ROOT / "include"
+NATIVE = PACKAGE_ROOT / "inference_performance_lab" / "_native"
+
+LIB_NAME = "libipl_b200.so"
+TORCH_OPS_NAME = "inference_performance_lab_cuda.so"
+
+# Stable ABI target: torch 2.10 (the oldest version that has every call the shim uses).
+TORCH_TARGET_VERSION = "0x020a000000000000"
+
+NVCC_FLAGS = [
+    "-gencode=arch=compute_100a,code=sm_100a",
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "-Xptxas=-v",
+    "-Xcompiler=-fPIC,-fvisibility=hidden",
+    "--expt-relaxed-constexpr",
+]
+
+
+def _nvcc() -> str:
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    candidate = Path(cuda_home) / "bin" / "nvcc"
+    if candidate.exists():
+        return str(candidate)
+    found = shutil.which("nvcc")
+    if found is None:
+        raise RuntimeError("nvcc not found; set CUDA_HOME")
+    return found
+
+
+def _stamp(sources: list[Path], flags: list[str]) -> str:
+    """Hash of the flags (repo paths made relative, so a moved checkout still matches) and sources."""
+    digest = hashlib.sha256()
+    for flag in flags:
+        digest.update(flag.replace(str(REPO_ROOT), "<repo>").encode())
+    for source in sources:
+        digest.update(source.read_bytes())
+    return digest.hexdigest()
+
+
+def _up_to_date(output: Path, stamp: str) -> bool:
+    stamp_file = output.with_suffix(output.suffix + ".stamp")
+    return output.exists() and stamp_file.exists() and stamp_file.read_text() == stamp
+
+
+def _write_stamp(output: Path, stamp: str) -> None:
+    output.with_suffix(output.suffix + ".stamp").write_text(stamp)
+
+
+def _run(command: list[str], verbose: bool) -> str:
+    if verbose:
+        print(" ".join(command), flush=True)
+    result = subprocess.run(command, capture_output=True, text=True)
+    if result.returncode != 0:
+        raise RuntimeError(
+            f"build command failed ({result.returncode}): {' '.join(command)}\n"
+            f"{result.stdout}\n{result.stderr}"
+        )
+    return result.stdout + result.stderr
+
+
+def build_native(verbose: bool = False) -> Path:
+    """Compile the CUDA kernels + C ABI into libipl_b200.so."""
+    NATIVE.mkdir(parents=True, exist_ok=True)
+    output = NATIVE / LIB_NAME
+    sources = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "ipl_b200.h"]
+    flags = [*NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}"]
+    stamp = _stamp(sources, flags)
+    if _up_to_date(output, stamp):
+        return output
+    command = [
+        _nvcc(),
+        *flags,
+        "-shared",
+        "-o",
+        str(output),
+        str(CSRC / "ipl_b200.cu"),
+    ]
+    log = _run(command, verbose)
+    (NATIVE / "libipl_b200.ptxas.txt").write_text(log)
+    _write_stamp(output, stamp)
+    return output
+
+
+def build_torch_ops(verbose: bool = False) -> Path:
+    """Compile the stable-ABI op registration, linked against libipl_b200.so."""
+    import torch
+
+    torch_root = Path(torch.__file__).resolve().parent
+    output = NATIVE / TORCH_OPS_NAME
+    sources = [CSRC / "torch_ops.cpp", INCLUDE / "ipl_b200.h"]
+    flags = [
+        "-O3",
+        "-std=c++17",
+        "-fPIC",
+        f"-DTORCH_TARGET_VERSION={TORCH_TARGET_VERSION}",
+        f"-I{torch_root / 'include'}",
+        f"-I{INCLUDE}",
+    ]
+    stamp = _stamp(sources + [NATIVE / LIB_NAME], flags)
+    if _up_to_date(output, stamp):
+        return output
+    command = [
+        os.environ.get("CXX", "g++"),
+        *flags,
+        "-shared",
+        "-o",
+        str(output),
+        str(CSRC / "torch_ops.cpp"),
+        f"-L{NATIVE}",
+        "-lipl_b200",
+        f"-L{torch_root / 'lib'}",
+        "-ltorch",
+        "-ltorch_cpu",
+        "-ltorch_cuda",
+        "-lc10",
+        "-Wl,-rpath,$ORIGIN",
+        f"-Wl,-rpath,{torch_root / 'lib'}",
+    ]
+    _run(command, verbose)
+    _write_stamp(output, stamp)
+    return output
+
+
+def build(verbose: bool = False) -> None:
+    """Build both libraries; concurrent callers (e.g. several ranks) serialise on a lock file."""
+    import fcntl
+
+    NATIVE.mkdir(parents=True, exist_ok=True)
+    with open(NATIVE / ".build.lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        try:
+            build_native(verbose)
+            build_torch_ops(verbose)
+        finally:
+            fcntl.flock(lock, fcntl.LOCK_UN)
+
+
+if __name__ == "__main__":
+    build(verbose="-q" not in sys.argv)

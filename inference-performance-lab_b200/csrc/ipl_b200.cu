@@ -1,0 +1,415 @@
+// C ABI of the library (declared in include/ipl_b200.h): argument checks, kernel selection and
+// launch. One translation unit holds every kernel so that the per-device fault word is a single
+// symbol without relocatable device code.
+#include "ipl_b200.h"
+
+#include "fused_add_rms_norm.cuh"
+#include "silu_and_mul.cuh"
+
+#include <atomic>
+#include <climits>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+namespace ipl {
+namespace {
+
+thread_local char t_last_error[512] = "";
+
+ipl_status fail(ipl_status status, const char* fmt, ...) {
+    va_list args;
+    va_start(args, fmt);
+    std::vsnprintf(t_last_error, sizeof(t_last_error), fmt, args);
+    va_end(args);
+    return status;
+}
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+    std::atomic<int> sm_count{0};
+    std::atomic<int> max_smem_optin{0};
+    std::atomic<uint32_t> smem_configured{0};  // bit per staged-kernel instance
+};
+DeviceInfo g_devices[kMaxDevices];
+
+// SM count and opt-in shared memory of the current device, queried once per device.
+ipl_status current_device(int* device, DeviceInfo** info) {
+    cudaError_t err = cudaGetDevice(device);
+    if (err != cudaSuccess) {
+        return fail(IPL_ERROR_CUDA, "failed to query the current CUDA device: %s", cudaGetErrorString(err));
+    }
+    if (*device < 0 || *device >= kMaxDevices) {
+        return fail(IPL_ERROR_CUDA, "CUDA device index %d is out of range", *device);
+    }
+    DeviceInfo& d = g_devices[*device];
+    if (d.sm_count.load(std::memory_order_acquire) == 0) {
+        int sms = 0, smem = 0;
+        err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, *device);
+        if (err == cudaSuccess) {
+            err = cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, *device);
+        }
+        if (err != cudaSuccess) {
+            return fail(IPL_ERROR_CUDA, "failed to read CUDA device properties: %s", cudaGetErrorString(err));
+        }
+        d.max_smem_optin.store(smem, std::memory_order_relaxed);
+        d.sm_count.store(sms, std::memory_order_release);
+    }
+    *info = &d;
+    return IPL_SUCCESS;
+}
+
+template <typename Kernel, typename... Args>
+cudaError_t launch(Kernel kernel, unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
+                   Args... args) {
+    // Programmatic stream serialisation: the kernel may be scheduled while the previous kernel
+    // in the stream drains; it orders its own global reads with griddepcontrol.wait.
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(grid);
+    config.blockDim = dim3(block);
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, kernel, args...);
+}
+
+// ------------------------------------------------------------------------------------------
+// add + RMSNorm planning
+
+enum class RmsKernel { kNone, kStaged1, kStaged2, kStaged4, kStaged8, kRowwiseCached, kRowwiseTwoPass };
+
+const char* rms_kernel_name(RmsKernel k) {
+    switch (k) {
+        case RmsKernel::kNone: return "none";
+        case RmsKernel::kStaged1: return "rmsnorm_staged_kernel<1>";
+        case RmsKernel::kStaged2: return "rmsnorm_staged_kernel<2>";
+        case RmsKernel::kStaged4: return "rmsnorm_staged_kernel<4>";
+        case RmsKernel::kStaged8: return "rmsnorm_staged_kernel<8>";
+        case RmsKernel::kRowwiseCached: return "rmsnorm_rowwise_kernel<cached>";
+        case RmsKernel::kRowwiseTwoPass: return "rmsnorm_rowwise_kernel<two-pass>";
+    }
+    return "invalid";
+}
+
+struct RmsPlan {
+    RmsKernel kernel = RmsKernel::kNone;
+    unsigned grid = 0;
+    size_t smem = 0;
+    StagedParams staged = {};
+};
+
+ipl_status check_rms_args(const void* x, const void* residual, const void* weight, int64_t rows,
+                          int64_t hidden, double epsilon) {
+    if (rows < 0) return fail(IPL_ERROR_INVALID_VALUE, "number of rows must be non-negative");
+    if (hidden <= 0) return fail(IPL_ERROR_INVALID_VALUE, "x must have a non-empty final dimension");
+    if (!(epsilon > 0.0)) return fail(IPL_ERROR_INVALID_VALUE, "epsilon must be positive");
+    if (hidden > INT_MAX) return fail(IPL_ERROR_TOO_LARGE, "hidden dimension is too large");
+    if (rows > INT_MAX) return fail(IPL_ERROR_TOO_LARGE, "number of rows is too large");
+    if (rows > 0 && (x == nullptr || residual == nullptr || weight == nullptr)) {
+        return fail(IPL_ERROR_INVALID_VALUE, "x, residual and weight must be non-null");
+    }
+    const uintptr_t odd = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(residual) |
+                          reinterpret_cast<uintptr_t>(weight);
+    if (odd & 1u) return fail(IPL_ERROR_INVALID_VALUE, "bfloat16 pointers must be 2-byte aligned");
+    if (rows > 0 && x == residual) return fail(IPL_ERROR_INVALID_VALUE, "x and residual must not alias");
+    return IPL_SUCCESS;
+}
+
+// Pure function of the arguments and two device limits.
+RmsPlan plan_rms(const void* x, const void* residual, int64_t rows, int64_t hidden, int sm_count,
+                 int smem_limit) {
+    RmsPlan plan;
+    if (rows == 0) return plan;
+    const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
+    const uintptr_t ra = reinterpret_cast<uintptr_t>(residual);
+    const int chunks_max = static_cast<int>((hidden + 7) / 8 + 1);
+    const int stage_bytes = ((2 * chunks_max * 16) + 127) & ~127;
+    const StagedLayout empty_layout = staged_layout(0, stage_bytes, chunks_max);
+    const int64_t room = static_cast<int64_t>(smem_limit) - empty_layout.total - 2 * 8 * kStagedMaxStages;
+    int max_stages = room > 0 ? static_cast<int>(room / stage_bytes) : 0;
+    if (max_stages > kStagedMaxStages) max_stages = kStagedMaxStages;
+
+    if ((xa & 15u) == (ra & 15u) && max_stages >= 2) {
+        const int grid = static_cast<int>(rows < sm_count ? rows : sm_count);
+        const int64_t rows_per_cta = (rows + grid - 1) / grid;
+        // Warps per row: enough groups to cover the rows of a CTA, no more.
+        int warps_per_row = rows_per_cta >= 8 ? 1 : rows_per_cta >= 4 ? 2 : rows_per_cta >= 2 ? 4 : 8;
+        while (kStagedConsumerWarps / warps_per_row > max_stages) warps_per_row *= 2;
+        const int groups = kStagedConsumerWarps / warps_per_row;
+        int stages = (max_stages / groups) * groups;
+        // No more stages than rows a CTA will ever hold at once.
+        const int64_t useful = ((rows_per_cta + groups - 1) / groups) * groups;
+        if (stages > useful) stages = static_cast<int>(useful);
+        plan.kernel = warps_per_row == 1   ? RmsKernel::kStaged1
+                      : warps_per_row == 2 ? RmsKernel::kStaged2
+                      : warps_per_row == 4 ? RmsKernel::kStaged4
+                                           : RmsKernel::kStaged8;
+        plan.grid = static_cast<unsigned>(grid);
+        plan.staged.rows = rows;
+        plan.staged.hidden = static_cast<int>(hidden);
+        plan.staged.chunks_max = chunks_max;
+        plan.staged.stage_bytes = stage_bytes;
+        plan.staged.stages = stages;
+        plan.staged.weight_phase = static_cast<int>((xa & 15u) >> 1);
+        plan.smem = staged_layout(stages, stage_bytes, chunks_max).total;
+        return plan;
+    }
+    plan.kernel = hidden <= static_cast<int64_t>(kRowwiseThreads) * kRowwiseCachedPerThread
+                      ? RmsKernel::kRowwiseCached
+                      : RmsKernel::kRowwiseTwoPass;
+    const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+    plan.grid = static_cast<unsigned>(rows < cap ? rows : cap);
+    return plan;
+}
+
+template <int W>
+ipl_status launch_staged(const RmsPlan& plan, DeviceInfo* info, int bit, cudaStream_t stream) {
+    auto kernel = rmsnorm_staged_kernel<W>;
+    if (!(info->smem_configured.load(std::memory_order_acquire) & (1u << bit))) {
+        const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     info->max_smem_optin.load());
+        if (err != cudaSuccess) {
+            return fail(IPL_ERROR_CUDA, "fused RMSNorm kernel setup failed: %s", cudaGetErrorString(err));
+        }
+        info->smem_configured.fetch_or(1u << bit, std::memory_order_acq_rel);
+    }
+    const cudaError_t err = launch(kernel, plan.grid, kStagedThreads, plan.smem, stream, plan.staged);
+    if (err != cudaSuccess) {
+        return fail(IPL_ERROR_CUDA, "fused RMSNorm kernel launch failed: %s", cudaGetErrorString(err));
+    }
+    return IPL_SUCCESS;
+}
+
+// ------------------------------------------------------------------------------------------
+// SiLU-and-mul planning
+
+enum class SiluKernel { kNone, kVector32, kVector16, kScalar };
+
+const char* silu_kernel_name(SiluKernel k) {
+    switch (k) {
+        case SiluKernel::kNone: return "none";
+        case SiluKernel::kVector32: return "silu_vector_kernel<32>";
+        case SiluKernel::kVector16: return "silu_vector_kernel<16>";
+        case SiluKernel::kScalar: return "silu_scalar_kernel";
+    }
+    return "invalid";
+}
+
+ipl_status check_silu_args(const void* output, const void* input, int64_t rows, int64_t inter) {
+    if (rows < 0 || inter < 0) return fail(IPL_ERROR_INVALID_VALUE, "sizes must be non-negative");
+    if (inter > (INT64_MAX / 4) || (inter > 0 && rows > INT64_MAX / (4 * inter))) {
+        return fail(IPL_ERROR_TOO_LARGE, "input is too large");
+    }
+    if (rows * inter > 0 && (output == nullptr || input == nullptr)) {
+        return fail(IPL_ERROR_INVALID_VALUE, "input and output must be non-null");
+    }
+    if ((reinterpret_cast<uintptr_t>(output) | reinterpret_cast<uintptr_t>(input)) & 1u) {
+        return fail(IPL_ERROR_INVALID_VALUE, "bfloat16 pointers must be 2-byte aligned");
+    }
+    return IPL_SUCCESS;
+}
+
+SiluKernel plan_silu(const void* output, const void* input, int64_t rows, int64_t inter) {
+    if (rows * inter == 0) return SiluKernel::kNone;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(output) | reinterpret_cast<uintptr_t>(input);
+    const uint64_t packs32 = static_cast<uint64_t>(rows) * static_cast<uint64_t>(inter / 16);
+    const uint64_t packs16 = static_cast<uint64_t>(rows) * static_cast<uint64_t>(inter / 8);
+    if (inter % 16 == 0 && (a & 31u) == 0 && packs32 <= UINT32_MAX) return SiluKernel::kVector32;
+    if (inter % 8 == 0 && (a & 15u) == 0 && packs16 <= UINT32_MAX) return SiluKernel::kVector16;
+    return SiluKernel::kScalar;
+}
+
+template <int kBytes>
+cudaError_t launch_silu_vector(uint16_t* out, const uint16_t* in, int64_t rows, int64_t inter,
+                               int sm_count, cudaStream_t stream) {
+    SiluVectorParams p;
+    p.out = out;
+    p.in = in;
+    p.intermediate = inter;
+    const uint32_t per_row = static_cast<uint32_t>(inter / (kBytes / 2));
+    p.total_packs = static_cast<uint32_t>(rows) * per_row;
+    p.packs_per_row = make_fast_div32(per_row);
+    // One wave: 8 CTAs of 256 threads per SM. Pick the smallest unroll that covers the work in
+    // that wave, up to 4, then loop.
+    const uint64_t wave = static_cast<uint64_t>(sm_count) * 8 * kSiluThreads;
+    const uint64_t total = p.total_packs;
+    if (total <= wave) {
+        const unsigned grid = static_cast<unsigned>((total + kSiluThreads - 1) / kSiluThreads);
+        return launch(silu_vector_kernel<kBytes, 1>, grid, kSiluThreads, 0, stream, p);
+    }
+    if (total <= 2 * wave) {
+        const unsigned grid = static_cast<unsigned>((total + 2 * kSiluThreads - 1) / (2 * kSiluThreads));
+        return launch(silu_vector_kernel<kBytes, 2>, grid, kSiluThreads, 0, stream, p);
+    }
+    const uint64_t need = (total + 4 * kSiluThreads - 1) / (4 * kSiluThreads);
+    const unsigned grid = static_cast<unsigned>(need < wave / kSiluThreads ? need : wave / kSiluThreads);
+    return launch(silu_vector_kernel<kBytes, 4>, grid, kSiluThreads, 0, stream, p);
+}
+
+ipl_status run_silu(void* output, const void* input, int64_t rows, int64_t inter, void* stream_ptr,
+                    bool packed_contract) {
+    ipl_status st = check_silu_args(output, input, rows, inter);
+    if (st != IPL_SUCCESS) return st;
+    if (rows * inter == 0) return IPL_SUCCESS;
+    if (packed_contract) {
+        if (inter % 8 != 0) return fail(IPL_ERROR_MISALIGNED, "the output width must be divisible by 8");
+        if ((reinterpret_cast<uintptr_t>(output) | reinterpret_cast<uintptr_t>(input)) & 15u) {
+            return fail(IPL_ERROR_MISALIGNED, "input and output must be 16-byte aligned");
+        }
+    }
+    int device = 0;
+    DeviceInfo* info = nullptr;
+    st = current_device(&device, &info);
+    if (st != IPL_SUCCESS) return st;
+    const int sms = info->sm_count.load(std::memory_order_relaxed);
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    auto* out = static_cast<uint16_t*>(output);
+    const auto* in = static_cast<const uint16_t*>(input);
+    cudaError_t err = cudaSuccess;
+    switch (plan_silu(output, input, rows, inter)) {
+        case SiluKernel::kVector32:
+            err = launch_silu_vector<32>(out, in, rows, inter, sms, stream);
+            break;
+        case SiluKernel::kVector16:
+            err = launch_silu_vector<16>(out, in, rows, inter, sms, stream);
+            break;
+        case SiluKernel::kScalar: {
+            const int64_t total = rows * inter;
+            const int64_t cap = static_cast<int64_t>(sms) * 8;
+            const int64_t need = (total + kSiluThreads - 1) / kSiluThreads;
+            err = launch(silu_scalar_kernel, static_cast<unsigned>(need < cap ? need : cap), kSiluThreads, 0,
+                         stream, out, in, rows, inter);
+            break;
+        }
+        case SiluKernel::kNone:
+            break;
+    }
+    if (err != cudaSuccess) {
+        return fail(IPL_ERROR_CUDA, "%s SiLU-and-multiply kernel launch failed: %s",
+                    packed_contract ? "packed" : "scalar", cudaGetErrorString(err));
+    }
+    return IPL_SUCCESS;
+}
+
+}  // namespace
+}  // namespace ipl
+
+using namespace ipl;
+
+extern "C" {
+
+ipl_status ipl_fused_add_rms_norm_bf16(void* x, void* residual, const void* weight, int64_t rows,
+                                       int64_t hidden_size, double epsilon, void* stream_ptr) {
+    ipl_status st = check_rms_args(x, residual, weight, rows, hidden_size, epsilon);
+    if (st != IPL_SUCCESS) return st;
+    if (rows == 0) return IPL_SUCCESS;
+    int device = 0;
+    DeviceInfo* info = nullptr;
+    st = current_device(&device, &info);
+    if (st != IPL_SUCCESS) return st;
+    RmsPlan plan = plan_rms(x, residual, rows, hidden_size, info->sm_count.load(std::memory_order_relaxed),
+                            info->max_smem_optin.load(std::memory_order_relaxed));
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    plan.staged.x = static_cast<uint16_t*>(x);
+    plan.staged.residual = static_cast<uint16_t*>(residual);
+    plan.staged.weight = static_cast<const uint16_t*>(weight);
+    plan.staged.epsilon = static_cast<float>(epsilon);
+    switch (plan.kernel) {
+        case RmsKernel::kStaged1: return launch_staged<1>(plan, info, 0, stream);
+        case RmsKernel::kStaged2: return launch_staged<2>(plan, info, 1, stream);
+        case RmsKernel::kStaged4: return launch_staged<4>(plan, info, 2, stream);
+        case RmsKernel::kStaged8: return launch_staged<8>(plan, info, 3, stream);
+        case RmsKernel::kRowwiseCached:
+        case RmsKernel::kRowwiseTwoPass: {
+            const cudaError_t err =
+                plan.kernel == RmsKernel::kRowwiseCached
+                    ? launch(rmsnorm_rowwise_kernel<true>, plan.grid, kRowwiseThreads, 0, stream,
+                             plan.staged.x, plan.staged.residual, plan.staged.weight, rows,
+                             static_cast<int>(hidden_size), plan.staged.epsilon)
+                    : launch(rmsnorm_rowwise_kernel<false>, plan.grid, kRowwiseThreads, 0, stream,
+                             plan.staged.x, plan.staged.residual, plan.staged.weight, rows,
+                             static_cast<int>(hidden_size), plan.staged.epsilon);
+            if (err != cudaSuccess) {
+                return fail(IPL_ERROR_CUDA, "fused RMSNorm kernel launch failed: %s", cudaGetErrorString(err));
+            }
+            return IPL_SUCCESS;
+        }
+        case RmsKernel::kNone:
+            return IPL_SUCCESS;
+    }
+    return IPL_SUCCESS;
+}
+
+ipl_status ipl_silu_and_mul_bf16(void* output, const void* input, int64_t rows, int64_t intermediate_size,
+                                 void* stream) {
+    return run_silu(output, input, rows, intermediate_size, stream, false);
+}
+
+ipl_status ipl_silu_and_mul_packed_bf16(void* output, const void* input, int64_t rows,
+                                        int64_t intermediate_size, void* stream) {
+    return run_silu(output, input, rows, intermediate_size, stream, true);
+}
+
+const char* ipl_last_error(void) { return t_last_error; }
+
+const char* ipl_status_string(ipl_status status) {
+    switch (status) {
+        case IPL_SUCCESS: return "IPL_SUCCESS";
+        case IPL_ERROR_INVALID_VALUE: return "IPL_ERROR_INVALID_VALUE";
+        case IPL_ERROR_MISALIGNED: return "IPL_ERROR_MISALIGNED";
+        case IPL_ERROR_TOO_LARGE: return "IPL_ERROR_TOO_LARGE";
+        case IPL_ERROR_CUDA: return "IPL_ERROR_CUDA";
+    }
+    return "IPL_UNKNOWN_STATUS";
+}
+
+int ipl_abi_version(void) { return IPL_ABI_VERSION; }
+
+ipl_status ipl_device_fault_flags(int device, uint32_t* flags) {
+    if (flags == nullptr) return fail(IPL_ERROR_INVALID_VALUE, "flags must be non-null");
+    int previous = 0;
+    cudaError_t err = cudaGetDevice(&previous);
+    if (err == cudaSuccess) err = cudaSetDevice(device);
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    if (err == cudaSuccess) err = cudaMemcpyFromSymbol(flags, g_fault_word, sizeof(uint32_t));
+    cudaSetDevice(previous);
+    if (err != cudaSuccess) {
+        return fail(IPL_ERROR_CUDA, "failed to read the device fault word: %s", cudaGetErrorString(err));
+    }
+    return IPL_SUCCESS;
+}
+
+ipl_status ipl_clear_device_fault_flags(int device) {
+    int previous = 0;
+    const uint32_t zero = 0;
+    cudaError_t err = cudaGetDevice(&previous);
+    if (err == cudaSuccess) err = cudaSetDevice(device);
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    if (err == cudaSuccess) err = cudaMemcpyToSymbol(g_fault_word, &zero, sizeof(uint32_t));
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    cudaSetDevice(previous);
+    if (err != cudaSuccess) {
+        return fail(IPL_ERROR_CUDA, "failed to clear the device fault word: %s", cudaGetErrorString(err));
+    }
+    return IPL_SUCCESS;
+}
+
+const char* ipl_fused_add_rms_norm_plan(const void* x, const void* residual, const void* weight, int64_t rows,
+                                        int64_t hidden_size) {
+    if (check_rms_args(x, residual, weight, rows, hidden_size, 1.0) != IPL_SUCCESS) return "invalid";
+    // B200 limits: 148 SMs, 232448 bytes of opt-in shared memory per block.
+    return rms_kernel_name(plan_rms(x, residual, rows, hidden_size, 148, 232448).kernel);
+}
+
+const char* ipl_silu_and_mul_plan(const void* output, const void* input, int64_t rows,
+                                  int64_t intermediate_size) {
+    if (check_silu_args(output, input, rows, intermediate_size) != IPL_SUCCESS) return "invalid";
+    return silu_kernel_name(plan_silu(output, input, rows, intermediate_size));
+}
+
+}  // extern "C"

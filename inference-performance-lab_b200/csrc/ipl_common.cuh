@@ -1,0 +1,197 @@
+// Device helpers shared by the add+RMSNorm and SiLU-and-mul kernels (sm_100a).
+//
+// bf16 is handled as raw 16-bit words: widening to fp32 is an exact shift, narrowing is the
+// hardware round-to-nearest-even convert (cvt.rn.bf16x2.f32), the same rounding torch applies in
+// Tensor.to(torch.bfloat16).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace ipl {
+
+constexpr int kWarpSize = 32;
+
+// Fault bits stored in the per-device fault word (see ipl_device_fault_flags).
+constexpr uint32_t kFaultFullBarrierTimeout = 1u << 0;   // a consumer never saw its stage fill
+constexpr uint32_t kFaultEmptyBarrierTimeout = 1u << 1;  // the producer never saw a stage drain
+
+// Bounded waits give up after this long (nanoseconds of %globaltimer). A stage fills within
+// microseconds on a healthy GPU; the bound only exists so that a lost copy ends the kernel
+// with a recorded fault instead of a hang.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// Per-device fault word (read by ipl_device_fault_flags). Defined here: the library is a single
+// translation unit (ipl_b200.cu includes every kernel header).
+__device__ uint32_t g_fault_word = 0;
+
+__device__ __forceinline__ float bf16_lo(uint32_t packed) { return __uint_as_float(packed << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t packed) { return __uint_as_float(packed & 0xffff0000u); }
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t bits) {
+    return __uint_as_float(static_cast<uint32_t>(bits) << 16);
+}
+
+// Two floats -> bf16x2 word (lo in bits 0..15), round to nearest even.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    uint32_t packed;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(hi), "f"(lo));
+    return packed;
+}
+__device__ __forceinline__ uint16_t float_to_bf16_bits(float value) {
+    return static_cast<uint16_t>(pack_bf16x2(value, 0.0f) & 0xffffu);
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---- global memory vectors -------------------------------------------------------------------
+
+struct alignas(16) U32x4 {
+    uint32_t v[4];
+};
+struct alignas(32) U32x8 {
+    uint32_t v[8];
+};
+
+// Streaming read-only loads: the data is used once, so keep it out of L1.
+__device__ __forceinline__ U32x4 ld_stream_v4(const void* p) {
+    U32x4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3])
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ U32x8 ld_stream_v8(const void* p) {
+    U32x8 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3]), "=r"(r.v[4]),
+                   "=r"(r.v[5]), "=r"(r.v[6]), "=r"(r.v[7])
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ void st_v4(void* p, const U32x4& r) {
+    asm volatile("st.global.v4.b32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(r.v[0]), "r"(r.v[1]),
+                 "r"(r.v[2]), "r"(r.v[3])
+                 : "memory");
+}
+__device__ __forceinline__ void st_v8(void* p, const U32x8& r) {
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(r.v[0]),
+                 "r"(r.v[1]), "r"(r.v[2]), "r"(r.v[3]), "r"(r.v[4]), "r"(r.v[5]), "r"(r.v[6]),
+                 "r"(r.v[7])
+                 : "memory");
+}
+
+// ---- shared memory ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ U32x4 lds_v4(uint32_t addr) {
+    U32x4 r;
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3])
+                 : "r"(addr));
+    return r;
+}
+__device__ __forceinline__ uint16_t lds_u16(uint32_t addr) {
+    uint16_t r;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(r) : "r"(addr));
+    return r;
+}
+
+// ---- mbarrier + bulk async copy (TMA, non-tensor form) ----------------------------------------
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Waits for the phase with the given parity to complete. Returns false (after recording
+// `fault_bit` in the device fault word) if it has not completed within kWaitLimitNs, or as soon
+// as *abort becomes nonzero (another warp of the CTA gave up).
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  volatile int* abort, uint32_t fault_bit) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = global_timer_ns();
+    for (uint32_t spin = 1;; ++spin) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((spin & 63u) == 0) {
+            if (*abort) return false;
+            if (global_timer_ns() - start > kWaitLimitNs) {
+                atomicOr(&g_fault_word, fault_bit);
+                *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// Bulk copy global -> shared (this CTA), completion counted on `bar` in bytes.
+// dst, src 16-byte aligned; bytes a multiple of 16. The L2 policy hint marks the source lines
+// evict-first: every byte is read exactly once.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
+// ---- named barriers + programmatic dependent launch ----------------------------------------
+
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Wait until the grid this launch depends on (the previous kernel in the stream, when launched
+// with programmatic stream serialisation) has completed and its writes are visible. A no-op
+// for a normal launch.
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Allow the next kernel in the stream to begin launching (its own dependency wait still orders
+// its reads after this grid's completion).
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float value) {
+#pragma unroll
+    for (int offset = kWarpSize / 2; offset > 0; offset >>= 1) {
+        value += __shfl_xor_sync(0xffffffffu, value, offset);
+    }
+    return value;
+}
+
+}  // namespace ipl

@@ -1,0 +1,130 @@
+// SiLU-and-multiply for sm_100a.
+//
+// out[r, c] = bf16(silu(g) * u), g = fp32(in[r, c]), u = fp32(in[r, I + c]), silu(g) = g / (1 + e^-g)
+// (reference: csrc/silu_and_mul_kernel.cu:30-81; oracle
+// src/inference_performance_lab/kernels/reference.py:26-35).
+//
+// * silu_vector_kernel<kBytes, kUnroll> - the aligned path. A 1-D grid over "packs" (kBytes of
+//   output = kBytes/2 elements, with the matching gate and up packs of the input). kBytes is 32
+//   (256-bit ld/st, sm_100) when the width and both pointers allow it, else 16. Each thread
+//   issues kUnroll pack loads before consuming any, so a single wave of CTAs keeps the whole
+//   working set in flight. Row/column of a pack come from a multiply-shift division by the
+//   packs-per-row constant (Granlund & Montgomery, "Division by Invariant Integers using
+//   Multiplication", PLDI 1994), computed once on the host.
+// * silu_scalar_kernel - any width, any alignment: one element per thread, coalesced 2-byte
+//   accesses over the flattened output.
+#pragma once
+
+#include "ipl_common.cuh"
+
+namespace ipl {
+
+constexpr int kSiluThreads = 256;
+
+// n / d for 32-bit n with a precomputed (multiplier, shift): q = (umulhi(n, m) + n) >> s.
+struct FastDiv32 {
+    uint32_t divisor;
+    uint32_t multiplier;
+    uint32_t shift;
+};
+
+inline FastDiv32 make_fast_div32(uint32_t d) {
+    FastDiv32 f;
+    f.divisor = d;
+    uint32_t l = 0;
+    while ((uint64_t{1} << l) < d) ++l;  // l = ceil(log2 d)
+    f.shift = l;
+    // m = floor(2^32 * (2^l - d) / d) + 1, fits in 32 bits for d >= 1.
+    f.multiplier = static_cast<uint32_t>(((uint64_t{1} << 32) * ((uint64_t{1} << l) - d)) / d + 1);
+    return f;
+}
+
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv32& f) {
+    const uint64_t t = static_cast<uint64_t>(__umulhi(n, f.multiplier)) + n;
+    return static_cast<uint32_t>(t >> f.shift);
+}
+
+__device__ __forceinline__ float silu_mul(float gate, float up) {
+    // gate * (1 / (1 + e^-gate)): e^-gate overflows to +inf for gate < -88, giving 0 * gate.
+    const float sig = __frcp_rn(__fadd_rn(1.0f, __expf(-gate)));
+    return __fmul_rn(__fmul_rn(gate, sig), up);
+}
+
+template <int kWords>
+__device__ __forceinline__ void silu_words(const uint32_t* g, const uint32_t* u, uint32_t* o) {
+#pragma unroll
+    for (int i = 0; i < kWords; ++i) {
+        o[i] = pack_bf16x2(silu_mul(bf16_lo(g[i]), bf16_lo(u[i])), silu_mul(bf16_hi(g[i]), bf16_hi(u[i])));
+    }
+}
+
+struct SiluVectorParams {
+    uint16_t* out;
+    const uint16_t* in;
+    int64_t intermediate;   // I
+    uint32_t total_packs;   // rows * packs_per_row
+    FastDiv32 packs_per_row;
+};
+
+template <int kBytes, int kUnroll>
+__global__ void __launch_bounds__(kSiluThreads) silu_vector_kernel(const SiluVectorParams p) {
+    constexpr int kElems = kBytes / 2;
+    constexpr int kWords = kBytes / 4;
+    using Vec = typename std::conditional<kBytes == 32, U32x8, U32x4>::type;
+    grid_dependency_wait();
+    grid_launch_dependents();
+
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t base = blockIdx.x * blockDim.x + threadIdx.x; base < p.total_packs;
+         base += stride * kUnroll) {
+        Vec gate[kUnroll], up[kUnroll];
+        int64_t out_off[kUnroll];
+#pragma unroll
+        for (int k = 0; k < kUnroll; ++k) {
+            const uint32_t pack = base + k * stride;
+            out_off[k] = -1;
+            if (pack < p.total_packs) {
+                const uint32_t row = fast_div(pack, p.packs_per_row);
+                const uint32_t col = pack - row * p.packs_per_row.divisor;
+                const int64_t in_off = static_cast<int64_t>(row) * 2 * p.intermediate + int64_t{col} * kElems;
+                out_off[k] = static_cast<int64_t>(row) * p.intermediate + int64_t{col} * kElems;
+                if constexpr (kBytes == 32) {
+                    gate[k] = ld_stream_v8(p.in + in_off);
+                    up[k] = ld_stream_v8(p.in + in_off + p.intermediate);
+                } else {
+                    gate[k] = ld_stream_v4(p.in + in_off);
+                    up[k] = ld_stream_v4(p.in + in_off + p.intermediate);
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kUnroll; ++k) {
+            if (out_off[k] >= 0) {
+                Vec o;
+                silu_words<kWords>(gate[k].v, up[k].v, o.v);
+                if constexpr (kBytes == 32) {
+                    st_v8(p.out + out_off[k], o);
+                } else {
+                    st_v4(p.out + out_off[k], o);
+                }
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kSiluThreads) silu_scalar_kernel(uint16_t* __restrict__ out,
+                                                                   const uint16_t* __restrict__ in,
+                                                                   int64_t rows, int64_t intermediate) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const int64_t total = rows * intermediate;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total; e += stride) {
+        const int64_t row = e / intermediate;
+        const int64_t col = e - row * intermediate;
+        const uint16_t* g = in + row * 2 * intermediate + col;
+        out[e] = float_to_bf16_bits(silu_mul(bf16_bits_to_float(g[0]), bf16_bits_to_float(g[intermediate])));
+    }
+}
+
+}  // namespace ipl

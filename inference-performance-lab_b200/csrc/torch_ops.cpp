@@ -1,0 +1,126 @@
+// Stable-LibTorch-ABI registration of the ops, a thin shim over the C ABI in ipl_b200.h.
+//
+// Namespace, schemas and in-place signatures are those of the reference
+// (csrc/torch_ops.cpp:12-22): fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual,
+// Tensor weight, float epsilon) -> (), silu_and_mul(Tensor(a!) output, Tensor input) -> (),
+// silu_and_mul_packed(Tensor(a!) output, Tensor input) -> (). The tensor checks repeat the
+// reference's (csrc/fused_add_rms_norm_kernel.cu:277-301, csrc/silu_and_mul_kernel.cu:86-106,
+// :130-158) with the same messages, so callers see the same RuntimeError texts. The kernel runs
+// on the current stream of the tensors' device, under a device guard; nothing synchronises.
+#include <torch/csrc/stable/accelerator.h>
+#include <torch/csrc/stable/library.h>
+#include <torch/csrc/stable/tensor.h>
+#include <torch/headeronly/core/ScalarType.h>
+#include <torch/headeronly/util/Exception.h>
+
+#include <cstdint>
+#include <limits>
+
+#include "ipl_b200.h"
+
+// Declared by torch's C shim under USE_CUDA; the symbol lives in libtorch_cuda.
+extern "C" AOTITorchError aoti_torch_get_current_cuda_stream(int32_t device_index, void** ret_stream);
+
+namespace ts = torch::stable;
+
+namespace {
+
+void* current_stream(int32_t device_index) {
+    void* stream = nullptr;
+    const AOTITorchError err = aoti_torch_get_current_cuda_stream(device_index, &stream);
+    STD_TORCH_CHECK(err == AOTI_TORCH_SUCCESS, "failed to query the current CUDA stream");
+    return stream;
+}
+
+void raise_on_error(ipl_status status) {
+    STD_TORCH_CHECK(status == IPL_SUCCESS, ipl_last_error());
+}
+
+void check_silu_tensors(const ts::Tensor& output, const ts::Tensor& input) {
+    STD_TORCH_CHECK(input.is_cuda() && output.is_cuda(), "input and output must be CUDA tensors");
+    STD_TORCH_CHECK(input.scalar_type() == torch::headeronly::ScalarType::BFloat16 &&
+                        output.scalar_type() == torch::headeronly::ScalarType::BFloat16,
+                    "input and output must use bfloat16");
+    STD_TORCH_CHECK(input.is_contiguous() && output.is_contiguous(), "input and output must be contiguous");
+    STD_TORCH_CHECK(input.device() == output.device(), "input and output must be on the same device");
+    STD_TORCH_CHECK(input.dim() >= 1 && input.size(-1) % 2 == 0, "the final input dimension must be even");
+    STD_TORCH_CHECK(output.dim() == input.dim(), "input and output must have the same rank");
+    const int64_t intermediate_size = input.size(-1) / 2;
+    STD_TORCH_CHECK(output.size(-1) == intermediate_size, "the output width must be half the input width");
+    for (int64_t dimension = 0; dimension < input.dim() - 1; ++dimension) {
+        STD_TORCH_CHECK(output.size(dimension) == input.size(dimension),
+                        "input and output leading dimensions must match");
+    }
+}
+
+void run_silu(ts::Tensor& output, const ts::Tensor& input, bool packed) {
+    check_silu_tensors(output, input);
+    if (output.numel() == 0) {
+        return;
+    }
+    const int64_t intermediate_size = input.size(-1) / 2;
+    const int64_t rows = output.numel() / intermediate_size;
+    const int32_t device = input.get_device_index();
+    const ts::accelerator::DeviceGuard device_guard(device);
+    void* stream = current_stream(device);
+    void* out = output.mutable_data_ptr();
+    const void* in = input.const_data_ptr();
+    raise_on_error(packed ? ipl_silu_and_mul_packed_bf16(out, in, rows, intermediate_size, stream)
+                          : ipl_silu_and_mul_bf16(out, in, rows, intermediate_size, stream));
+}
+
+}  // namespace
+
+void fused_add_rms_norm_cuda(ts::Tensor& x, ts::Tensor& residual, const ts::Tensor& weight, double epsilon) {
+    STD_TORCH_CHECK(x.is_cuda(), "x must be a CUDA tensor");
+    STD_TORCH_CHECK(residual.is_cuda(), "residual must be a CUDA tensor");
+    STD_TORCH_CHECK(weight.is_cuda(), "weight must be a CUDA tensor");
+
+    STD_TORCH_CHECK(x.scalar_type() == torch::headeronly::ScalarType::BFloat16, "x must use bfloat16");
+    STD_TORCH_CHECK(residual.scalar_type() == torch::headeronly::ScalarType::BFloat16, "residual must use bfloat16");
+    STD_TORCH_CHECK(weight.scalar_type() == torch::headeronly::ScalarType::BFloat16, "weight must use bfloat16");
+
+    STD_TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
+    STD_TORCH_CHECK(residual.is_contiguous(), "residual must be contiguous");
+    STD_TORCH_CHECK(weight.is_contiguous(), "weight must be contiguous");
+
+    STD_TORCH_CHECK(x.sizes().equals(residual.sizes()), "x and residual must have identical shapes");
+    STD_TORCH_CHECK(x.device() == residual.device() && x.device() == weight.device(),
+                    "x, residual, and weight must be on the same device");
+    STD_TORCH_CHECK(x.dim() >= 1, "x must have at least one dimension");
+    STD_TORCH_CHECK(weight.dim() == 1, "weight must be one-dimensional");
+    STD_TORCH_CHECK(weight.size(0) == x.size(-1), "weight must match the final tensor dimension");
+    STD_TORCH_CHECK(epsilon > 0.0, "epsilon must be positive");
+
+    const int64_t hidden_size = x.size(-1);
+    if (x.numel() == 0) {
+        // Nothing to normalise (the reference launches an empty grid here and fails).
+        return;
+    }
+    const int64_t rows = x.numel() / hidden_size;
+
+    STD_TORCH_CHECK(hidden_size <= std::numeric_limits<int>::max(), "hidden dimension is too large");
+    STD_TORCH_CHECK(rows <= std::numeric_limits<int>::max(), "number of rows is too large");
+
+    const int32_t device = x.get_device_index();
+    const ts::accelerator::DeviceGuard device_guard(device);
+    void* stream = current_stream(device);
+    raise_on_error(ipl_fused_add_rms_norm_bf16(x.mutable_data_ptr(), residual.mutable_data_ptr(),
+                                               weight.const_data_ptr(), rows, hidden_size, epsilon, stream));
+}
+
+void silu_and_mul_cuda(ts::Tensor& output, const ts::Tensor& input) { run_silu(output, input, false); }
+
+void silu_and_mul_packed_cuda(ts::Tensor& output, const ts::Tensor& input) { run_silu(output, input, true); }
+
+STABLE_TORCH_LIBRARY(inference_performance_lab, library) {
+    library.def("fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor weight, float epsilon) -> ()");
+    library.def("silu_and_mul(Tensor(a!) output, Tensor input) -> ()");
+    library.def("silu_and_mul_packed(Tensor(a!) output, Tensor input) -> ()");
+}
+
+STABLE_TORCH_LIBRARY_IMPL(inference_performance_lab, CUDA, library) {
+    library.impl("fused_add_rms_norm", TORCH_BOX(&fused_add_rms_norm_cuda));
+    library.impl("silu_and_mul", TORCH_BOX(&silu_and_mul_cuda));
+    library.impl("silu_and_mul_packed", TORCH_BOX(&silu_and_mul_packed_cuda));
+}

@@ -1,0 +1,80 @@
+"""vLLM general plugin: the ``inference_lab`` provider of ``vllm.ir.ops.fused_add_rms_norm``.
+
+Same entry point, provider name and registration as the reference
+(src/inference_performance_lab/kernels/vllm_plugin.py:11,43-69; entry point
+``vllm.general_plugins: inference_performance_lab = ...vllm_plugin:register``, pyproject.toml:39-40).
+The argument filter is wider: the reference accepted only 2-D inputs with hidden size 3584
+(:15-40, the one shape its specialised kernel handled); the B200 kernels take any hidden size and
+alignment, so any contiguous bf16 input on one CUDA device with a weight and no
+``variance_size`` is accepted.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from inference_performance_lab.kernels.extension import (
+    fused_add_rms_norm as custom_fused_add_rms_norm,
+)
+from inference_performance_lab.kernels.extension import load_extension
+
+PROVIDER = "inference_lab"
+
+
+def supports_fused_add_rms_norm(
+    x: Tensor,
+    x_residual: Tensor,
+    weight: Tensor | None,
+    epsilon: float,
+    variance_size: int | None = None,
+) -> bool:
+    del epsilon
+
+    return (
+        variance_size is None
+        and weight is not None
+        and x.device.type == "cuda"
+        and x_residual.device == x.device
+        and weight.device == x.device
+        and x.dtype == torch.bfloat16
+        and x_residual.dtype == x.dtype
+        and weight.dtype == x.dtype
+        and x.ndim >= 1
+        and x.shape == x_residual.shape
+        and x.shape[-1] > 0
+        and weight.shape == (x.shape[-1],)
+        and x.is_contiguous()
+        and x_residual.is_contiguous()
+        and weight.is_contiguous()
+        and x.data_ptr() != x_residual.data_ptr()
+    )
+
+
+def register() -> None:
+    from vllm import ir
+
+    op = ir.ops.fused_add_rms_norm
+    if PROVIDER in op.impls:
+        return
+
+    load_extension()
+
+    @op.register_impl(
+        PROVIDER,
+        supported=torch.cuda.is_available(),
+        supports_args=supports_fused_add_rms_norm,
+        inplace=True,
+    )
+    def inference_lab_fused_add_rms_norm(
+        x: Tensor,
+        x_residual: Tensor,
+        weight: Tensor | None,
+        epsilon: float,
+        variance_size: int | None = None,
+    ) -> tuple[Tensor, Tensor]:
+        assert weight is not None
+        assert variance_size is None
+
+        custom_fused_add_rms_norm(x, x_residual, weight, epsilon)
+        return x, x_residual

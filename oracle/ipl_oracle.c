@@ -1,0 +1,87 @@
+/*
+ * CPU oracle (TEST INFRASTRUCTURE ONLY: used by tests/, the smoke check and the CPU-baseline leg
+ * of bench.py as the checker; never by the product path).
+ *
+ * Plain-C restatement of the reference's fp32 oracle,
+ * src/inference_performance_lab/kernels/reference.py of sreeganeshji/inference-performance-lab:
+ *
+ *   fused_add_rms_norm_reference (reference.py:7-23):
+ *     residual_out_fp32 = x.float() + residual.float()                       (:18)
+ *     inverse_rms = rsqrt(residual_out_fp32.square().mean(-1) + epsilon)     (:19)
+ *     output = residual_out_fp32 * inverse_rms * weight.float()              (:21)
+ *     return output.to(bf16), residual_out_fp32.to(bf16)                     (:23)
+ *
+ *   silu_and_mul_reference (reference.py:26-35):
+ *     gate, up = x.float().chunk(2, -1); output = silu(gate) * up; output.to(bf16)  (:32-35)
+ *
+ * Rounding: every fp32 operation rounds to nearest (compile with -ffp-contract=off so no FMA
+ * contraction changes a product). bf16 narrowing is round-to-nearest-even with NaN -> 0x7FC0,
+ * as c10::BFloat16 does. The mean of squares is accumulated in double and rounded once to fp32,
+ * which is at least as accurate as torch's fp32 cascade sum; the normalised output can therefore
+ * differ from torch's by one bf16 ulp in rare elements (within the tests' tolerance), while the
+ * residual output is exact.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+static inline float bf16_to_f32(uint16_t bits) {
+    uint32_t u = (uint32_t)bits << 16;
+    float f;
+    memcpy(&f, &u, sizeof f);
+    return f;
+}
+
+static inline uint16_t f32_to_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, sizeof u);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)0x7fc0u;
+    const uint32_t bias = 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)((u + bias) >> 16);
+}
+
+uint16_t oracle_f32_to_bf16(float f) { return f32_to_bf16(f); }
+float oracle_bf16_to_f32(uint16_t b) { return bf16_to_f32(b); }
+
+/* Returns 0, or -1 if the scratch row could not be allocated. */
+int oracle_fused_add_rms_norm_bf16(const uint16_t* x, const uint16_t* residual, const uint16_t* weight,
+                                   int64_t rows, int64_t hidden, double epsilon, uint16_t* out,
+                                   uint16_t* residual_out) {
+    if (rows <= 0 || hidden <= 0) return 0;
+    float* v = (float*)malloc(sizeof(float) * (size_t)hidden);
+    if (v == NULL) return -1;
+    const float eps = (float)epsilon;
+    for (int64_t r = 0; r < rows; ++r) {
+        const uint16_t* xr = x + r * hidden;
+        const uint16_t* rr = residual + r * hidden;
+        double acc = 0.0;
+        for (int64_t c = 0; c < hidden; ++c) {
+            const float value = bf16_to_f32(xr[c]) + bf16_to_f32(rr[c]);
+            const float square = value * value;
+            v[c] = value;
+            residual_out[r * hidden + c] = f32_to_bf16(value);
+            acc += (double)square;
+        }
+        const float mean = (float)(acc / (double)hidden);
+        const float inverse_rms = 1.0f / sqrtf(mean + eps);
+        for (int64_t c = 0; c < hidden; ++c) {
+            const float scaled = v[c] * inverse_rms;
+            out[r * hidden + c] = f32_to_bf16(scaled * bf16_to_f32(weight[c]));
+        }
+    }
+    free(v);
+    return 0;
+}
+
+void oracle_silu_and_mul_bf16(const uint16_t* input, int64_t rows, int64_t intermediate, uint16_t* out) {
+    for (int64_t r = 0; r < rows; ++r) {
+        const uint16_t* gate = input + r * 2 * intermediate;
+        const uint16_t* up = gate + intermediate;
+        for (int64_t c = 0; c < intermediate; ++c) {
+            const float g = bf16_to_f32(gate[c]);
+            const float silu = g / (1.0f + expf(-g));
+            out[r * intermediate + c] = f32_to_bf16(silu * bf16_to_f32(up[c]));
+        }
+    }
+}

@@ -1,0 +1,144 @@
+"""The C-ABI library without a GPU: it loads, exports every declared symbol, validates arguments
+before touching the device, and its kernel selection (a pure function of pointers and sizes)
+picks the intended path for each shape and alignment of the parity and bench cases."""
+
+from __future__ import annotations
+
+import re
+from pathlib import Path
+
+import pytest
+
+from inference_performance_lab.kernels import capi
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "ipl_b200.h"
+
+# Fake, never-dereferenced device addresses: 256-byte aligned base plus an element offset.
+BASE = 0x7F0000000000
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*IPL_API\s+[\w\s*]*?\b(ipl_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_path_entry_points() -> None:
+    names = declared_functions()
+    for required in (
+        "ipl_fused_add_rms_norm_bf16",
+        "ipl_silu_and_mul_bf16",
+        "ipl_silu_and_mul_packed_bf16",
+        "ipl_last_error",
+    ):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol() -> None:
+    lib = capi.library()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert set(declared_functions()) == set(capi.SIGNATURES)
+
+
+def test_abi_version_and_status_strings() -> None:
+    lib = capi.library()
+    assert lib.ipl_abi_version() == 1
+    assert lib.ipl_status_string(capi.IPL_ERROR_MISALIGNED) == b"IPL_ERROR_MISALIGNED"
+    assert lib.ipl_status_string(99) == b"IPL_UNKNOWN_STATUS"
+
+
+@pytest.mark.parametrize(
+    "args, status, message",
+    [
+        ((BASE, BASE + 4096, BASE + 8192, 4, 3584, 0.0), capi.IPL_ERROR_INVALID_VALUE, "epsilon must be positive"),
+        ((BASE, BASE + 4096, BASE + 8192, 4, 3584, -1.0), capi.IPL_ERROR_INVALID_VALUE, "epsilon must be positive"),
+        ((BASE, BASE + 4096, BASE + 8192, 4, 0, 1e-6), capi.IPL_ERROR_INVALID_VALUE, "non-empty final dimension"),
+        ((BASE, BASE + 4096, BASE + 8192, -1, 16, 1e-6), capi.IPL_ERROR_INVALID_VALUE, "non-negative"),
+        ((0, BASE + 4096, BASE + 8192, 4, 16, 1e-6), capi.IPL_ERROR_INVALID_VALUE, "non-null"),
+        ((BASE, BASE, BASE + 8192, 4, 16, 1e-6), capi.IPL_ERROR_INVALID_VALUE, "must not alias"),
+        ((BASE + 1, BASE + 4096, BASE + 8192, 4, 16, 1e-6), capi.IPL_ERROR_INVALID_VALUE, "2-byte aligned"),
+        ((BASE, BASE + 4096, BASE + 8192, 4, 2**31, 1e-6), capi.IPL_ERROR_TOO_LARGE, "hidden dimension is too large"),
+        ((BASE, BASE + 4096, BASE + 8192, 2**31, 16, 1e-6), capi.IPL_ERROR_TOO_LARGE, "number of rows is too large"),
+    ],
+)
+def test_rms_argument_errors(args, status, message) -> None:
+    with pytest.raises(capi.IplError, match=message) as info:
+        capi.fused_add_rms_norm(*args)
+    assert info.value.status == status
+
+
+def test_rms_empty_batch_is_a_no_op() -> None:
+    # rows == 0 returns before any device query.
+    capi.fused_add_rms_norm(0, 0, 0, 0, 3584, 1e-6)
+
+
+@pytest.mark.parametrize(
+    "fn, args, status, message",
+    [
+        (capi.silu_and_mul_packed, (BASE, BASE + 4096, 4, 18), capi.IPL_ERROR_MISALIGNED,
+         "the output width must be divisible by 8"),
+        (capi.silu_and_mul_packed, (BASE + 2, BASE + 4096, 4, 16), capi.IPL_ERROR_MISALIGNED,
+         "input and output must be 16-byte aligned"),
+        (capi.silu_and_mul_packed, (BASE, BASE + 4098, 4, 16), capi.IPL_ERROR_MISALIGNED,
+         "input and output must be 16-byte aligned"),
+        (capi.silu_and_mul, (0, BASE, 4, 16), capi.IPL_ERROR_INVALID_VALUE, "non-null"),
+        (capi.silu_and_mul, (BASE, BASE + 4096, -1, 16), capi.IPL_ERROR_INVALID_VALUE, "non-negative"),
+        (capi.silu_and_mul, (BASE + 1, BASE + 4096, 1, 16), capi.IPL_ERROR_INVALID_VALUE, "2-byte aligned"),
+        (capi.silu_and_mul, (BASE, BASE + 4096, 2**40, 2**40), capi.IPL_ERROR_TOO_LARGE, "too large"),
+    ],
+)
+def test_silu_argument_errors(fn, args, status, message) -> None:
+    with pytest.raises(capi.IplError, match=message) as info:
+        fn(*args)
+    assert info.value.status == status
+
+
+def test_silu_empty_is_a_no_op() -> None:
+    capi.silu_and_mul(0, 0, 0, 18944)
+    capi.silu_and_mul_packed(0, 0, 128, 0)
+
+
+def rms_plan(x_off: int, r_off: int, w_off: int, rows: int, hidden: int) -> str:
+    # Offsets in bf16 elements from 256-byte aligned bases.
+    return capi.fused_add_rms_norm_plan(
+        BASE + 2 * x_off, BASE + (1 << 34) + 2 * r_off, BASE + (1 << 35) + 2 * w_off, rows, hidden
+    )
+
+
+def test_rms_plan_selection() -> None:
+    # 2048 x 3584 aligned (the bench workload): one warp per row, rows streamed through stages.
+    assert rms_plan(0, 0, 0, 2048, 3584) == "rmsnorm_staged_kernel<1>"
+    # Same with x and residual both one element off 16 bytes: the same staged kernel.
+    assert rms_plan(1, 1, 0, 2048, 3584) == "rmsnorm_staged_kernel<1>"
+    # Only one of them misaligned (the reference's misaligned tests): the general row kernel.
+    assert rms_plan(1, 0, 0, 8, 3584) == "rmsnorm_rowwise_kernel<cached>"
+    assert rms_plan(0, 1, 0, 8, 3584) == "rmsnorm_rowwise_kernel<cached>"
+    # A misaligned weight does not matter: gamma is staged in shared memory.
+    assert rms_plan(0, 0, 1, 8, 3584).startswith("rmsnorm_staged_kernel")
+    # Few rows: more warps share a row.
+    assert rms_plan(0, 0, 0, 1, 3584) == "rmsnorm_staged_kernel<8>"
+    assert rms_plan(0, 0, 0, 148 * 2, 3584) == "rmsnorm_staged_kernel<4>"
+    assert rms_plan(0, 0, 0, 148 * 4, 3584) == "rmsnorm_staged_kernel<2>"
+    # The row-sharded workload's hidden size.
+    assert rms_plan(0, 0, 0, 262144, 8192).startswith("rmsnorm_staged_kernel")
+    assert rms_plan(0, 0, 0, 32768, 8192).startswith("rmsnorm_staged_kernel")
+    # Odd widths stay on the staged kernel when x and residual share their offset.
+    assert rms_plan(0, 0, 0, 64, 1001).startswith("rmsnorm_staged_kernel")
+    # Rows too long for two stages fall back to the two-pass row kernel.
+    assert rms_plan(0, 0, 0, 64, 40000) == "rmsnorm_rowwise_kernel<two-pass>"
+    assert rms_plan(1, 0, 0, 64, 40000) == "rmsnorm_rowwise_kernel<two-pass>"
+    assert rms_plan(0, 0, 0, 0, 3584) == "none"
+    assert rms_plan(0, 0, 0, 4, 0) == "invalid"
+
+
+def silu_plan(out_off: int, in_off: int, rows: int, inter: int) -> str:
+    return capi.silu_and_mul_plan(BASE + 2 * out_off, BASE + (1 << 34) + 2 * in_off, rows, inter)
+
+
+def test_silu_plan_selection() -> None:
+    assert silu_plan(0, 0, 128, 18944) == "silu_vector_kernel<32>"
+    assert silu_plan(8, 0, 128, 18944) == "silu_vector_kernel<16>"
+    assert silu_plan(0, 0, 128, 18952) == "silu_vector_kernel<16>"
+    assert silu_plan(0, 0, 3, 1001) == "silu_scalar_kernel"
+    assert silu_plan(1, 0, 128, 18944) == "silu_scalar_kernel"
+    assert silu_plan(0, 0, 0, 18944) == "none"
