@@ -117,8 +117,8 @@ class ClockSampler:
             try:
                 import torch
 
-                bus = torch.cuda.get_device_properties(device_index).pci_bus_id
-                handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode() if isinstance(bus, str) else bus)
+                props = torch.cuda.get_device_properties(device_index)
+                handle = pynvml.nvmlDeviceGetHandleByUUID(f"GPU-{props.uuid}")
             except Exception:
                 visible = os.environ.get("CUDA_VISIBLE_DEVICES")
                 index = int(visible.split(",")[device_index]) if visible else device_index
@@ -429,6 +429,14 @@ def run_ours(args, spec) -> None:
 
         e2e = run_e2e(args, spec, rows, batches, weight if not is_silu else None, stream, dist)
 
+    # Every bounded wait of the staged kernel must have completed: a nonzero fault word means a
+    # kernel gave up and its outputs are incomplete, so the run is not a measurement.
+    from inference_performance_lab.kernels import capi
+
+    fault_flags = int(dist.max(float(capi.device_fault_flags(dist.local_rank))))
+    if fault_flags:
+        raise SystemExit(f"device fault word {fault_flags:#x}: a kernel gave up on a wait")
+
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         sample_rows = spec["rows"] if not spec.get("sharded") else 1024
@@ -479,6 +487,7 @@ def run_ours(args, spec) -> None:
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": args.steps,
+        "fault_flags": fault_flags,
         "clocks": clocks.summary(),
     }
     if dist.rank == 0:

@@ -54,6 +54,20 @@ def _nvcc() -> str:
     return found
 
 
+def _host_cxx() -> str:
+    """The system C++ compiler, whose libstdc++ is the shared one torch itself uses.
+
+    The shim throws C++ exceptions (std::runtime_error from STD_TORCH_CHECK) into torch's
+    dispatcher, so it must share torch's libstdc++.so.6. A compiler that links its own static
+    libstdc++ (as the one named by $CXX in some images does) embeds and exports a second copy,
+    and building an exception message through it crashes inside the host process.
+    """
+    for candidate in ("/usr/bin/g++", shutil.which("g++")):
+        if candidate and Path(candidate).exists():
+            return candidate
+    raise RuntimeError("g++ not found")
+
+
 def _stamp(sources: list[Path], flags: list[str]) -> str:
     """Hash of the flags (repo paths made relative, so a moved checkout still matches) and sources."""
     digest = hashlib.sha256()
@@ -127,7 +141,7 @@ def build_torch_ops(verbose: bool = False) -> Path:
     if _up_to_date(output, stamp):
         return output
     command = [
-        os.environ.get("CXX", "g++"),
+        _host_cxx(),
         *flags,
         "-shared",
         "-o",

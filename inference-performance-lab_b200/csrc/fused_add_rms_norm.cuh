@@ -33,9 +33,10 @@
 
 namespace ipl {
 
-constexpr int kStagedConsumerWarps = 8;
+constexpr int kStagedConsumerWarps = 16;
 constexpr int kStagedThreads = (kStagedConsumerWarps + 1) * kWarpSize;  // + 1 producer warp
 constexpr int kStagedMaxStages = 32;
+constexpr int kStagedUnroll = 2;  // chunks per thread in flight between shared-memory loads and use
 constexpr int kRowwiseThreads = 256;
 constexpr int kRowwiseCachedPerThread = 16;  // rows up to 4096 elements keep v in registers
 
@@ -47,36 +48,46 @@ struct StagedParams {
     int hidden;
     int chunks_max;     // 16-byte chunks in one staged row (covers any phase)
     int stage_bytes;    // bytes of one stage: x span then residual span
-    int stages;         // ring depth; a multiple of the number of consumer groups, so that stage
-                        // s is always consumed by group s % groups, in round order
-    int weight_phase;   // element shift applied to gamma in shared memory (uniform phase only)
+    int stages;         // ring depth S (any value >= 1; see the consumer's wait)
+    int row_phase;      // element offset of row 0 of x (and residual) inside its 16-byte chunk
+    int shift_weight;   // 1: gamma's own phase differs from row_phase, build a shifted copy
     float epsilon;
 };
 
-// Shared memory map (dynamic): [stages * stage_bytes][gamma: chunks_max*16 bytes]
-//                              [full barriers][empty barriers][reduction partials][abort flag]
+// Shared memory map (dynamic):
+//   [stages * stage_bytes]      staged rows (x span, then residual span)
+//   [chunks_max * 16]           gamma as copied (16-byte aligned span around the weight)
+//   [chunks_max * 16]           gamma shifted to the rows' phase (only if shift_weight)
+//   [2 * stages + 1] mbarriers  S full, S empty, 1 gamma
+//   [2 * 16 floats]             cross-warp partial sums (two parities)
+//   [kStagedMaxStages ints]     per-stage count of warp releases (W per consumed row)
+//   [16 bytes]                  abort flag
 struct StagedLayout {
-    uint32_t weight_offset;
+    uint32_t weight_raw_offset;
+    uint32_t weight_shifted_offset;
     uint32_t barrier_offset;
     uint32_t reduce_offset;
+    uint32_t released_offset;
     uint32_t abort_offset;
     uint32_t total;
 };
 
-__host__ __device__ inline StagedLayout staged_layout(int stages, int stage_bytes, int chunks_max) {
+__host__ __device__ inline StagedLayout staged_layout(int stages, int stage_bytes, int chunks_max,
+                                                      int shift_weight) {
     StagedLayout l;
-    l.weight_offset = static_cast<uint32_t>(stages) * static_cast<uint32_t>(stage_bytes);
-    l.barrier_offset = l.weight_offset + static_cast<uint32_t>(chunks_max) * 16u;
-    l.barrier_offset = (l.barrier_offset + 15u) & ~15u;
-    l.reduce_offset = l.barrier_offset + 2u * 8u * static_cast<uint32_t>(stages);
-    // partials: [2 parities][kStagedConsumerWarps] floats
-    l.abort_offset = l.reduce_offset + 2u * kStagedConsumerWarps * 4u;
+    const uint32_t span = static_cast<uint32_t>(chunks_max) * 16u;
+    l.weight_raw_offset = static_cast<uint32_t>(stages) * static_cast<uint32_t>(stage_bytes);
+    l.weight_shifted_offset = l.weight_raw_offset + span;
+    l.barrier_offset = l.weight_shifted_offset + (shift_weight ? span : 0u);
+    l.reduce_offset = l.barrier_offset + 8u * (2u * static_cast<uint32_t>(stages) + 1u);
+    l.released_offset = l.reduce_offset + 2u * kStagedConsumerWarps * 4u;
+    l.abort_offset = l.released_offset + 4u * kStagedMaxStages;
     l.total = l.abort_offset + 16u;
     return l;
 }
 
 // Processes the 8 elements of one 16-byte chunk. `first` is the row column of element 0 of the
-// chunk (may be negative, or run past H, for the partial first and last chunks).
+// chunk (negative, or running past H, for the partial first and last chunks).
 template <bool kPass2>
 __device__ __forceinline__ void staged_chunk(const U32x4& xs, const U32x4& rs, const U32x4& ws,
                                              int first, int hidden, float inv, float& sumsq,
@@ -89,8 +100,8 @@ __device__ __forceinline__ void staged_chunk(const U32x4& xs, const U32x4& rs, c
         if constexpr (!kPass2) {
             const bool ok0 = full || (first + 2 * i >= 0 && first + 2 * i < hidden);
             const bool ok1 = full || (first + 2 * i + 1 >= 0 && first + 2 * i + 1 < hidden);
-            sumsq += ok0 ? __fmul_rn(v0, v0) : 0.0f;
-            sumsq += ok1 ? __fmul_rn(v1, v1) : 0.0f;
+            sumsq = fmaf(ok0 ? v0 : 0.0f, ok0 ? v0 : 0.0f, sumsq);
+            sumsq = fmaf(ok1 ? v1 : 0.0f, ok1 ? v1 : 0.0f, sumsq);
             out.v[i] = pack_bf16x2(v0, v1);
         } else {
             const float o0 = __fmul_rn(__fmul_rn(v0, inv), bf16_lo(ws.v[i]));
@@ -113,20 +124,48 @@ __device__ __forceinline__ void store_partial_chunk(uint16_t* chunk_base, const 
     }
 }
 
+__device__ __forceinline__ void store_chunk(uint16_t* chunk_base, const U32x4& out, bool full, int first,
+                                            int hidden) {
+    if (full) {
+        st_v4(chunk_base, out);
+    } else {
+        store_partial_chunk(chunk_base, out, first, hidden);
+    }
+}
+
+// Gamma for chunk k: 8 bf16 from shared memory. With shift 0 it is one aligned 16-byte load;
+// otherwise (rows whose phase differs from the staged gamma's, only when H % 8 != 0) it is
+// gathered element by element, zero outside the staged span.
+__device__ __forceinline__ U32x4 weight_chunk(uint32_t weight_base, int k, int shift, int span) {
+    if (shift == 0) return lds_v4(weight_base + 16u * k);
+    U32x4 ws;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int i0 = 8 * k + 2 * i - shift;
+        const uint32_t lo = (i0 >= 0 && i0 < span) ? lds_u16(weight_base + 2u * i0) : 0u;
+        const uint32_t hi = (i0 + 1 >= 0 && i0 + 1 < span) ? lds_u16(weight_base + 2u * (i0 + 1)) : 0u;
+        ws.v[i] = lo | (hi << 16);
+    }
+    return ws;
+}
+
 template <int kWarpsPerRow>
 __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const StagedParams p) {
     static_assert(kStagedConsumerWarps % kWarpsPerRow == 0, "groups must tile the consumer warps");
     constexpr int kGroups = kStagedConsumerWarps / kWarpsPerRow;
     constexpr int kGroupThreads = kWarpsPerRow * kWarpSize;
+    constexpr int kConsumerThreads = kStagedConsumerWarps * kWarpSize;
 
     extern __shared__ __align__(128) unsigned char smem[];
-    const StagedLayout layout = staged_layout(p.stages, p.stage_bytes, p.chunks_max);
+    const StagedLayout layout = staged_layout(p.stages, p.stage_bytes, p.chunks_max, p.shift_weight);
     const uint32_t smem_base = smem_addr(smem);
     const uint32_t full_bar = smem_base + layout.barrier_offset;
     const uint32_t empty_bar = full_bar + 8u * static_cast<uint32_t>(p.stages);
+    const uint32_t weight_bar = empty_bar + 8u * static_cast<uint32_t>(p.stages);
     float* partials = reinterpret_cast<float*>(smem + layout.reduce_offset);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + layout.abort_offset);
-    uint16_t* weight_smem = reinterpret_cast<uint16_t*>(smem + layout.weight_offset);
+    int* released = reinterpret_cast<int*>(smem + layout.released_offset);
+    const uint32_t half = static_cast<uint32_t>(p.chunks_max) * 16u;
 
     const int warp = threadIdx.x / kWarpSize;
     const int lane = threadIdx.x % kWarpSize;
@@ -141,6 +180,8 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
             mbar_init(full_bar + 8u * s, 1);
             mbar_init(empty_bar + 8u * s, kWarpsPerRow);
         }
+        mbar_init(weight_bar, 1);
+        for (int s = 0; s < p.stages; ++s) released[s] = 0;
         *abort = 0;
         fence_mbar_init();
     }
@@ -149,11 +190,21 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
     // Every input may have been written by the previous kernel in the stream.
     grid_dependency_wait();
 
+    const uintptr_t wa = reinterpret_cast<uintptr_t>(p.weight);
+    const int weight_phase = static_cast<int>((wa & 15u) >> 1);
+
     if (warp == kStagedConsumerWarps) {
-        // ---------------- producer: one elected thread issues all row copies ----------------
+        // ---------------- producer: one elected thread issues every bulk copy ----------------
         if (lane == 0) {
+            // Gamma: the 16-byte aligned span around it, once per CTA.
+            const uintptr_t wbase = wa & ~static_cast<uintptr_t>(15);
+            const uint32_t wbytes =
+                (static_cast<uint32_t>(wa - wbase) + 2u * static_cast<uint32_t>(p.hidden) + 15u) & ~15u;
+            mbar_arrive_expect_tx(weight_bar, wbytes);
+            bulk_load(smem_base + layout.weight_raw_offset, reinterpret_cast<const void*>(wbase), wbytes,
+                      weight_bar, l2_policy_evict_last());
+
             const uint64_t policy = l2_policy_evict_first();
-            const uint32_t half = static_cast<uint32_t>(p.chunks_max) * 16u;
             for (int j = 0; j < local_rows; ++j) {
                 const int s = j % p.stages;
                 const int round = j / p.stages;
@@ -171,42 +222,57 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
                 const uint32_t chunks = (phase + static_cast<uint32_t>(p.hidden) + 7u) >> 3;
                 const uint32_t bytes = chunks * 16u;
                 const uint32_t stage = smem_base + static_cast<uint32_t>(s) * p.stage_bytes;
-                mbar_arrive_expect_tx(full_bar + 8u * s, 2u * bytes);
-                bulk_load(stage, reinterpret_cast<const void*>(xbase), bytes, full_bar + 8u * s, policy);
-                bulk_load(stage + half, reinterpret_cast<const void*>(rbase), bytes, full_bar + 8u * s,
-                          policy);
+                const uint32_t bar = full_bar + 8u * static_cast<uint32_t>(s);
+                mbar_arrive_expect_tx(bar, 2u * bytes);
+                bulk_load(stage, reinterpret_cast<const void*>(xbase), bytes, bar, policy);
+                bulk_load(stage + half, reinterpret_cast<const void*>(rbase), bytes, bar, policy);
             }
         }
         return;
     }
 
     // ---------------- consumers ----------------
-    // Stage gamma once per CTA, shifted by the row phase so that chunk k of a staged row lines
-    // up with bytes [16k, 16k+16) of weight_smem. Elements outside [0, H) are zero.
-    {
-        const int span = p.chunks_max * 8;
-        const uint16_t* w = p.weight;
-        for (int i = threadIdx.x; i < span; i += kStagedConsumerWarps * kWarpSize) {
-            const int column = i - p.weight_phase;
-            weight_smem[i] = (column >= 0 && column < p.hidden) ? w[column] : static_cast<uint16_t>(0);
+    const int span = p.chunks_max * 8;
+    if (!mbar_wait_bounded(weight_bar, 0, abort, kFaultFullBarrierTimeout)) return;
+    // Gamma index of row column c is c + gamma_phase in the staged copy.
+    int gamma_phase = weight_phase;
+    uint32_t weight_base = smem_base + layout.weight_raw_offset;
+    if (p.shift_weight) {
+        // Re-stage gamma with the rows' phase so that chunk k of a row lines up with bytes
+        // [16k, 16k + 16) of the copy.
+        const uint16_t* raw = reinterpret_cast<const uint16_t*>(smem + layout.weight_raw_offset);
+        uint16_t* shifted = reinterpret_cast<uint16_t*>(smem + layout.weight_shifted_offset);
+        for (int i = threadIdx.x; i < span; i += kConsumerThreads) {
+            const int src = i - p.row_phase + weight_phase;
+            shifted[i] = (src >= 0 && src < span) ? raw[src] : static_cast<uint16_t>(0);
         }
-        named_barrier_sync(1, kStagedConsumerWarps * kWarpSize);
+        named_barrier_sync(1, kConsumerThreads);
+        gamma_phase = p.row_phase;
+        weight_base = smem_base + layout.weight_shifted_offset;
     }
     grid_launch_dependents();
 
     const int group = warp / kWarpsPerRow;
     const int warp_in_group = warp % kWarpsPerRow;
-    const int thread_in_group = threadIdx.x % kGroupThreads;
-    const uint32_t half = static_cast<uint32_t>(p.chunks_max) * 16u;
-    const uint32_t weight_base = smem_base + layout.weight_offset;
-    const float inv_hidden_den = static_cast<float>(p.hidden);
+    const int t = threadIdx.x % kGroupThreads;
+    const float hidden_f = static_cast<float>(p.hidden);
 
     int parity_slot = 0;
     for (int j = group; j < local_rows; j += kGroups) {
+        // Row j lives in stage s = j % S, round r = j / S. A phase-parity wait on the stage's
+        // full barrier is exact only if the barrier is in phase r: round r - 1 (row j - S, held
+        // by whichever group got it) must be complete, and round r + 1 cannot be, since row
+        // j + S is loaded only after this group releases row j. Bulk copies may complete out of
+        // issue order, so round r - 1's completion is established from its release count, not
+        // from load order: once all W warps of its group released row j - S, it was loaded.
         const int s = j % p.stages;
-        if (!mbar_wait_bounded(full_bar + 8u * s, (j / p.stages) & 1, abort, kFaultFullBarrierTimeout)) {
+        const int round = j / p.stages;
+        if (round > 0 && !spin_until_at_least(released + s, round * kWarpsPerRow, abort,
+                                              kFaultFullBarrierTimeout)) {
             break;
         }
+        const uint32_t bar = full_bar + 8u * static_cast<uint32_t>(s);
+        if (!mbar_wait_bounded(bar, round & 1, abort, kFaultFullBarrierTimeout)) break;
         const int64_t row = row_begin + j;
         const uintptr_t xa = reinterpret_cast<uintptr_t>(p.x + row * p.hidden);
         const uintptr_t ra = reinterpret_cast<uintptr_t>(p.residual + row * p.hidden);
@@ -215,22 +281,29 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
         const int phase = static_cast<int>((xa & 15u) >> 1);
         const int chunks = (phase + p.hidden + 7) >> 3;
         const uint32_t stage = smem_base + static_cast<uint32_t>(s) * p.stage_bytes;
-        // Gamma index of chunk k is shifted by (phase - weight_phase) elements; with a uniform
-        // phase the shift is 0 and the 16-byte gamma load is aligned.
-        const int weight_shift = phase - p.weight_phase;
+        const int weight_shift = phase - gamma_phase;
 
-        // Pass 1: residual out + sum of squares.
+        // Pass 1: residual out + sum of squares (kStagedUnroll chunks loaded before use).
         float sumsq = 0.0f;
-        for (int k = thread_in_group; k < chunks; k += kGroupThreads) {
-            const U32x4 xs = lds_v4(stage + 16u * k);
-            const U32x4 rs = lds_v4(stage + half + 16u * k);
-            U32x4 out;
-            bool full;
-            staged_chunk<false>(xs, rs, xs, 8 * k - phase, p.hidden, 0.0f, sumsq, out, full);
-            if (full) {
-                st_v4(rbase + 8 * k, out);
-            } else {
-                store_partial_chunk(rbase + 8 * k, out, 8 * k - phase, p.hidden);
+        for (int k0 = t; k0 < chunks; k0 += kGroupThreads * kStagedUnroll) {
+            U32x4 xs[kStagedUnroll], rs[kStagedUnroll];
+#pragma unroll
+            for (int u = 0; u < kStagedUnroll; ++u) {
+                const int k = k0 + u * kGroupThreads;
+                if (k < chunks) {
+                    xs[u] = lds_v4(stage + 16u * k);
+                    rs[u] = lds_v4(stage + half + 16u * k);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kStagedUnroll; ++u) {
+                const int k = k0 + u * kGroupThreads;
+                if (k < chunks) {
+                    U32x4 out;
+                    bool full;
+                    staged_chunk<false>(xs[u], rs[u], xs[u], 8 * k - phase, p.hidden, 0.0f, sumsq, out, full);
+                    store_chunk(rbase + 8 * k, out, full, 8 * k - phase, p.hidden);
+                }
             }
         }
         sumsq = warp_sum(sumsq);
@@ -243,39 +316,38 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
             for (int w = 0; w < kWarpsPerRow; ++w) sumsq += slot[w];
             parity_slot ^= 1;
         }
-        const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, inv_hidden_den) + p.epsilon);
+        const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
 
-        // Pass 2: normalised output.
-        for (int k = thread_in_group; k < chunks; k += kGroupThreads) {
-            const U32x4 xs = lds_v4(stage + 16u * k);
-            const U32x4 rs = lds_v4(stage + half + 16u * k);
-            U32x4 ws;
-            if (weight_shift == 0) {
-                ws = lds_v4(weight_base + 16u * k);
-            } else {
+        // Pass 2: normalised output, v recomputed from the staged bytes.
+        for (int k0 = t; k0 < chunks; k0 += kGroupThreads * kStagedUnroll) {
+            U32x4 xs[kStagedUnroll], rs[kStagedUnroll], ws[kStagedUnroll];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int i0 = 8 * k + 2 * i - weight_shift;
-                    const uint32_t lo = (i0 >= 0 && i0 < p.chunks_max * 8)
-                                            ? lds_u16(weight_base + 2u * i0) : 0u;
-                    const uint32_t hi = (i0 + 1 >= 0 && i0 + 1 < p.chunks_max * 8)
-                                            ? lds_u16(weight_base + 2u * (i0 + 1)) : 0u;
-                    ws.v[i] = lo | (hi << 16);
+            for (int u = 0; u < kStagedUnroll; ++u) {
+                const int k = k0 + u * kGroupThreads;
+                if (k < chunks) {
+                    xs[u] = lds_v4(stage + 16u * k);
+                    rs[u] = lds_v4(stage + half + 16u * k);
+                    ws[u] = weight_chunk(weight_base, k, weight_shift, span);
                 }
             }
-            U32x4 out;
-            bool full;
-            float unused = 0.0f;
-            staged_chunk<true>(xs, rs, ws, 8 * k - phase, p.hidden, inv, unused, out, full);
-            if (full) {
-                st_v4(xbase + 8 * k, out);
-            } else {
-                store_partial_chunk(xbase + 8 * k, out, 8 * k - phase, p.hidden);
+#pragma unroll
+            for (int u = 0; u < kStagedUnroll; ++u) {
+                const int k = k0 + u * kGroupThreads;
+                if (k < chunks) {
+                    U32x4 out;
+                    bool full;
+                    float unused = 0.0f;
+                    staged_chunk<true>(xs[u], rs[u], ws[u], 8 * k - phase, p.hidden, inv, unused, out, full);
+                    store_chunk(xbase + 8 * k, out, full, 8 * k - phase, p.hidden);
+                }
             }
         }
         // Release the stage: every lane of this warp has finished reading it.
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar + 8u * s);
+        if (lane == 0) {
+            atomicAdd(released + s, 1);
+            mbar_arrive(empty_bar + 8u * s);
+        }
     }
 }
 

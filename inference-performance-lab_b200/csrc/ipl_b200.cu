@@ -81,7 +81,16 @@ cudaError_t launch(Kernel kernel, unsigned grid, unsigned block, size_t smem, cu
 // ------------------------------------------------------------------------------------------
 // add + RMSNorm planning
 
-enum class RmsKernel { kNone, kStaged1, kStaged2, kStaged4, kStaged8, kRowwiseCached, kRowwiseTwoPass };
+enum class RmsKernel {
+    kNone,
+    kStaged1,
+    kStaged2,
+    kStaged4,
+    kStaged8,
+    kStaged16,
+    kRowwiseCached,
+    kRowwiseTwoPass
+};
 
 const char* rms_kernel_name(RmsKernel k) {
     switch (k) {
@@ -90,6 +99,7 @@ const char* rms_kernel_name(RmsKernel k) {
         case RmsKernel::kStaged2: return "rmsnorm_staged_kernel<2>";
         case RmsKernel::kStaged4: return "rmsnorm_staged_kernel<4>";
         case RmsKernel::kStaged8: return "rmsnorm_staged_kernel<8>";
+        case RmsKernel::kStaged16: return "rmsnorm_staged_kernel<16>";
         case RmsKernel::kRowwiseCached: return "rmsnorm_rowwise_kernel<cached>";
         case RmsKernel::kRowwiseTwoPass: return "rmsnorm_rowwise_kernel<two-pass>";
     }
@@ -121,42 +131,68 @@ ipl_status check_rms_args(const void* x, const void* residual, const void* weigh
 }
 
 // Pure function of the arguments and two device limits.
-RmsPlan plan_rms(const void* x, const void* residual, int64_t rows, int64_t hidden, int sm_count,
-                 int smem_limit) {
+RmsPlan plan_rms(const void* x, const void* residual, const void* weight, int64_t rows, int64_t hidden,
+                 int sm_count, int smem_limit) {
     RmsPlan plan;
     if (rows == 0) return plan;
     const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
     const uintptr_t ra = reinterpret_cast<uintptr_t>(residual);
+    const uintptr_t wa = reinterpret_cast<uintptr_t>(weight);
     const int chunks_max = static_cast<int>((hidden + 7) / 8 + 1);
-    const int stage_bytes = ((2 * chunks_max * 16) + 127) & ~127;
-    const StagedLayout empty_layout = staged_layout(0, stage_bytes, chunks_max);
-    const int64_t room = static_cast<int64_t>(smem_limit) - empty_layout.total - 2 * 8 * kStagedMaxStages;
-    int max_stages = room > 0 ? static_cast<int>(room / stage_bytes) : 0;
+    const int stage_bytes = 2 * chunks_max * 16;
+    const int row_phase = static_cast<int>((xa & 15u) >> 1);
+    // Gamma needs a shifted copy when every row has one phase (H % 8 == 0) and gamma's differs.
+    const int shift_weight = (hidden % 8 == 0 && row_phase != static_cast<int>((wa & 15u) >> 1)) ? 1 : 0;
+    const StagedLayout fixed = staged_layout(0, stage_bytes, chunks_max, shift_weight);
+    const int64_t room = static_cast<int64_t>(smem_limit) - fixed.total;
+    int max_stages = room > 0 ? static_cast<int>(room / (stage_bytes + 2 * 8)) : 0;
     if (max_stages > kStagedMaxStages) max_stages = kStagedMaxStages;
 
     if ((xa & 15u) == (ra & 15u) && max_stages >= 2) {
         const int grid = static_cast<int>(rows < sm_count ? rows : sm_count);
         const int64_t rows_per_cta = (rows + grid - 1) / grid;
-        // Warps per row: enough groups to cover the rows of a CTA, no more.
-        int warps_per_row = rows_per_cta >= 8 ? 1 : rows_per_cta >= 4 ? 2 : rows_per_cta >= 2 ? 4 : 8;
-        while (kStagedConsumerWarps / warps_per_row > max_stages) warps_per_row *= 2;
-        const int groups = kStagedConsumerWarps / warps_per_row;
-        int stages = (max_stages / groups) * groups;
-        // No more stages than rows a CTA will ever hold at once.
-        const int64_t useful = ((rows_per_cta + groups - 1) / groups) * groups;
-        if (stages > useful) stages = static_cast<int>(useful);
+        // Ring depth S and consumer groups G (W = 16 / G warps per row), from a sweep of both on
+        // B200 (2048..262144 rows, H 1024..8192):
+        // * a CTA whose rows all fit in shared memory at once takes them all (S = its rows) and
+        //   processes up to 8 at a time: the kernel is then bound by its start-up and drain, and
+        //   having every row requested at the start shortens both;
+        // * a CTA that streams more rows than fit keeps about 128 KB in flight with one stage per
+        //   group (S = G): 4 x 32 KB rows at H = 8192 ran at 97 % of the copy peak, deeper rings
+        //   at 91 %.
+        int stages;
+        int groups;
+        if (rows_per_cta <= max_stages) {
+            stages = static_cast<int>(rows_per_cta);
+            groups = stages >= 8 ? 8 : stages >= 4 ? 4 : stages >= 2 ? 2 : 1;
+        } else {
+            const int target = static_cast<int>((128 * 1024 + stage_bytes / 2) / stage_bytes);
+            groups = 1;
+            while (groups * 2 <= target && groups * 2 <= kStagedConsumerWarps && groups * 2 <= max_stages) {
+                groups *= 2;
+            }
+            stages = groups;
+        }
+#ifdef IPL_TUNING_FORCE_GROUPS
+        groups = IPL_TUNING_FORCE_GROUPS;
+#endif
+#ifdef IPL_TUNING_FORCE_STAGES
+        if (stages > IPL_TUNING_FORCE_STAGES) stages = IPL_TUNING_FORCE_STAGES;
+#endif
+        const int warps_per_row = kStagedConsumerWarps / groups;
         plan.kernel = warps_per_row == 1   ? RmsKernel::kStaged1
                       : warps_per_row == 2 ? RmsKernel::kStaged2
                       : warps_per_row == 4 ? RmsKernel::kStaged4
-                                           : RmsKernel::kStaged8;
+                      : warps_per_row == 8 ? RmsKernel::kStaged8
+                                           : RmsKernel::kStaged16;
         plan.grid = static_cast<unsigned>(grid);
         plan.staged.rows = rows;
         plan.staged.hidden = static_cast<int>(hidden);
         plan.staged.chunks_max = chunks_max;
         plan.staged.stage_bytes = stage_bytes;
         plan.staged.stages = stages;
-        plan.staged.weight_phase = static_cast<int>((xa & 15u) >> 1);
-        plan.smem = staged_layout(stages, stage_bytes, chunks_max).total;
+        plan.staged.row_phase = row_phase;
+        plan.staged.shift_weight = shift_weight;
+        plan.smem = staged_layout(stages, stage_bytes, chunks_max, shift_weight).total;
         return plan;
     }
     plan.kernel = hidden <= static_cast<int64_t>(kRowwiseThreads) * kRowwiseCachedPerThread
@@ -312,7 +348,8 @@ ipl_status ipl_fused_add_rms_norm_bf16(void* x, void* residual, const void* weig
     DeviceInfo* info = nullptr;
     st = current_device(&device, &info);
     if (st != IPL_SUCCESS) return st;
-    RmsPlan plan = plan_rms(x, residual, rows, hidden_size, info->sm_count.load(std::memory_order_relaxed),
+    RmsPlan plan = plan_rms(x, residual, weight, rows, hidden_size,
+                            info->sm_count.load(std::memory_order_relaxed),
                             info->max_smem_optin.load(std::memory_order_relaxed));
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     plan.staged.x = static_cast<uint16_t*>(x);
@@ -324,6 +361,7 @@ ipl_status ipl_fused_add_rms_norm_bf16(void* x, void* residual, const void* weig
         case RmsKernel::kStaged2: return launch_staged<2>(plan, info, 1, stream);
         case RmsKernel::kStaged4: return launch_staged<4>(plan, info, 2, stream);
         case RmsKernel::kStaged8: return launch_staged<8>(plan, info, 3, stream);
+        case RmsKernel::kStaged16: return launch_staged<16>(plan, info, 4, stream);
         case RmsKernel::kRowwiseCached:
         case RmsKernel::kRowwiseTwoPass: {
             const cudaError_t err =
@@ -403,7 +441,7 @@ const char* ipl_fused_add_rms_norm_plan(const void* x, const void* residual, con
                                         int64_t hidden_size) {
     if (check_rms_args(x, residual, weight, rows, hidden_size, 1.0) != IPL_SUCCESS) return "invalid";
     // B200 limits: 148 SMs, 232448 bytes of opt-in shared memory per block.
-    return rms_kernel_name(plan_rms(x, residual, rows, hidden_size, 148, 232448).kernel);
+    return rms_kernel_name(plan_rms(x, residual, weight, rows, hidden_size, 148, 232448).kernel);
 }
 
 const char* ipl_silu_and_mul_plan(const void* output, const void* input, int64_t rows,

@@ -151,6 +151,26 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     }
 }
 
+// Spins (with the same bound) until the shared counter reaches `target`.
+__device__ __forceinline__ bool spin_until_at_least(const int* counter, int target, volatile int* abort,
+                                                    uint32_t fault_bit) {
+    const volatile int* c = counter;
+    if (*c >= target) return true;
+    const uint64_t start = global_timer_ns();
+    for (uint32_t spin = 1;; ++spin) {
+        if (*c >= target) return true;
+        if ((spin & 63u) == 0) {
+            if (*abort) return false;
+            if (global_timer_ns() - start > kWaitLimitNs) {
+                atomicOr(&g_fault_word, fault_bit);
+                *abort = 1;
+                return false;
+            }
+        }
+        __nanosleep(32);
+    }
+}
+
 // Bulk copy global -> shared (this CTA), completion counted on `bar` in bytes.
 // dst, src 16-byte aligned; bytes a multiple of 16. The L2 policy hint marks the source lines
 // evict-first: every byte is read exactly once.
@@ -161,6 +181,11 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
         "[%0], [%1], %2, [%3], %4;" ::"r"(dst),
         "l"(src), "r"(bytes), "r"(bar), "l"(policy)
         : "memory");
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
 }
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t policy;

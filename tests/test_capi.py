@@ -106,22 +106,26 @@ def rms_plan(x_off: int, r_off: int, w_off: int, rows: int, hidden: int) -> str:
 
 
 def test_rms_plan_selection() -> None:
-    # 2048 x 3584 aligned (the bench workload): one warp per row, rows streamed through stages.
-    assert rms_plan(0, 0, 0, 2048, 3584) == "rmsnorm_staged_kernel<1>"
+    # 2048 x 3584 aligned (the bench workload): all 14 rows of a CTA in flight, 8 groups of 2
+    # warps.
+    assert rms_plan(0, 0, 0, 2048, 3584) == "rmsnorm_staged_kernel<2>"
     # Same with x and residual both one element off 16 bytes: the same staged kernel.
-    assert rms_plan(1, 1, 0, 2048, 3584) == "rmsnorm_staged_kernel<1>"
+    assert rms_plan(1, 1, 0, 2048, 3584) == "rmsnorm_staged_kernel<2>"
     # Only one of them misaligned (the reference's misaligned tests): the general row kernel.
     assert rms_plan(1, 0, 0, 8, 3584) == "rmsnorm_rowwise_kernel<cached>"
     assert rms_plan(0, 1, 0, 8, 3584) == "rmsnorm_rowwise_kernel<cached>"
     # A misaligned weight does not matter: gamma is staged in shared memory.
     assert rms_plan(0, 0, 1, 8, 3584).startswith("rmsnorm_staged_kernel")
     # Few rows: more warps share a row.
-    assert rms_plan(0, 0, 0, 1, 3584) == "rmsnorm_staged_kernel<8>"
-    assert rms_plan(0, 0, 0, 148 * 2, 3584) == "rmsnorm_staged_kernel<4>"
-    assert rms_plan(0, 0, 0, 148 * 4, 3584) == "rmsnorm_staged_kernel<2>"
-    # The row-sharded workload's hidden size.
-    assert rms_plan(0, 0, 0, 262144, 8192).startswith("rmsnorm_staged_kernel")
-    assert rms_plan(0, 0, 0, 32768, 8192).startswith("rmsnorm_staged_kernel")
+    assert rms_plan(0, 0, 0, 1, 3584) == "rmsnorm_staged_kernel<16>"
+    assert rms_plan(0, 0, 0, 148 * 2, 3584) == "rmsnorm_staged_kernel<8>"
+    assert rms_plan(0, 0, 0, 148 * 4, 3584) == "rmsnorm_staged_kernel<4>"
+    # Streaming (more rows than fit): about 128 KB in flight, one stage per group.
+    assert rms_plan(0, 0, 0, 148 * 16, 3584) == "rmsnorm_staged_kernel<2>"
+    assert rms_plan(0, 0, 0, 148 * 64, 1024) == "rmsnorm_staged_kernel<1>"
+    # The row-sharded workload's hidden size: four 32 KB rows in flight, 4 warps each.
+    assert rms_plan(0, 0, 0, 262144, 8192) == "rmsnorm_staged_kernel<4>"
+    assert rms_plan(0, 0, 0, 32768, 8192) == "rmsnorm_staged_kernel<4>"
     # Odd widths stay on the staged kernel when x and residual share their offset.
     assert rms_plan(0, 0, 0, 64, 1001).startswith("rmsnorm_staged_kernel")
     # Rows too long for two stages fall back to the two-pass row kernel.

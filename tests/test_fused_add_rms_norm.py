@@ -260,6 +260,45 @@ def test_back_to_back_calls_chain_correctly() -> None:
     assert torch.equal(xk, xg) and torch.equal(rk, rg)
 
 
+@pytest.mark.parametrize("rows, hidden", [(32768, 8192), (2048, 3584), (4096, 1024)])
+@torch.inference_mode()
+def test_chained_launches_after_copies_and_in_graphs(rows: int, hidden: int) -> None:
+    """Launch patterns of real callers: after host-to-device copies into the same buffers, and
+    as a chain of in-place calls replayed from a CUDA graph. Every call must complete (the
+    device fault word stays 0) and the chain must equal the same calls made one at a time."""
+    capi.clear_device_fault_flags(torch.cuda.current_device())
+    torch.manual_seed(6)
+    x_h = torch.randn(rows, hidden, dtype=torch.bfloat16).pin_memory()
+    r_h = torch.randn(rows, hidden, dtype=torch.bfloat16).pin_memory()
+    w = (torch.randn(hidden, device="cuda") * 0.1 + 1).to(torch.bfloat16)
+    x = torch.empty(rows, hidden, device="cuda", dtype=torch.bfloat16)
+    r = torch.empty_like(x)
+    for _ in range(3):
+        x.copy_(x_h, non_blocking=True)
+        r.copy_(r_h, non_blocking=True)
+        custom_fused_add_rms_norm(x, r, w, EPSILON)
+    torch.cuda.synchronize()
+    if rows * hidden <= 8 * 2**20:
+        check(x_h, r_h, w, EPSILON, x, r, "after copies")
+
+    x_ref, r_ref = x.clone(), r.clone()
+    for _ in range(8):
+        custom_fused_add_rms_norm(x_ref, r_ref, w, EPSILON)
+        torch.cuda.synchronize()
+    xg, rg = x.clone(), r.clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(8):
+            custom_fused_add_rms_norm(xg, rg, w, EPSILON)
+    xg.copy_(x)
+    rg.copy_(r)
+    graph.replay()
+    torch.cuda.synchronize()
+    del graph
+    assert torch.equal(xg, x_ref) and torch.equal(rg, r_ref)
+    assert capi.device_fault_flags(torch.cuda.current_device()) == 0
+
+
 @torch.inference_mode()
 def test_empty_and_error_cases() -> None:
     w = torch.ones(3584, device="cuda", dtype=torch.bfloat16)

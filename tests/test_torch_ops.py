@@ -56,3 +56,28 @@ def test_vllm_provider_registers_and_filters_arguments() -> None:
     w = torch.ones(3584, dtype=torch.bfloat16)
     # CPU tensors are never routed to the CUDA provider.
     assert not vllm_plugin.supports_fused_add_rms_norm(x, x.clone(), w, 1e-6)
+
+
+def test_shim_shares_torchs_libstdcxx() -> None:
+    """The op library throws C++ exceptions into torch's dispatcher, so it must use the shared
+    libstdc++ that torch uses and export no copy of its own (a statically linked libstdc++
+    crashed while formatting the first error message)."""
+    import shutil
+    import subprocess
+
+    extension.ensure_built()
+    if shutil.which("nm") is None:
+        pytest.skip("binutils nm unavailable")
+    exported = subprocess.run(
+        ["nm", "-D", "--defined-only", str(extension.TORCH_OPS_LIBRARY)],
+        capture_output=True, text=True, check=True,
+    ).stdout.split()
+    # Inline template instantiations (weak symbols) are normal; the library's own copy of the
+    # stream / locale machinery is not.
+    bundled = [s for s in exported if any(k in s for k in ("codecvt", "ios_base", "locale", "_ZNSo"))]
+    assert not bundled, bundled[:5]
+    assert len(exported) < 100
+    needed = subprocess.run(
+        ["readelf", "-d", str(extension.TORCH_OPS_LIBRARY)], capture_output=True, text=True, check=True
+    ).stdout
+    assert "libstdc++.so.6" in needed
