@@ -428,6 +428,7 @@ def run_ours(args, spec) -> None:
         del graph
 
         e2e = run_e2e(args, spec, rows, batches, weight if not is_silu else None, stream, dist)
+        same_traffic = copy_same_traffic(spec, rows, device, args.steps)
 
     # Every bounded wait of the staged kernel must have completed: a nonzero fault word means a
     # kernel gave up and its outputs are incomplete, so the run is not a measurement.
@@ -447,8 +448,9 @@ def run_ours(args, spec) -> None:
     value = total_bytes / (ms_per_step * 1e-3) / 1e9
     peak, peak_kind = load_peak()
     achieved = per_step / (local_ms / args.steps * 1e-3) / 1e9
-    key = args.workload
-    traffic = load_traffic(key)
+    traffic = load_traffic(args.workload)
+    if traffic is not None:
+        traffic = traffic * rows / WORKLOADS[args.workload]["rows"]
     total_rows = rows * dist.world if not spec.get("sharded") else spec["rows"]
     line = {
         "metric": "add+RMSNorm achieved HBM GB/s" if not is_silu else "SiLU-and-mul achieved GB/s",
@@ -483,6 +485,8 @@ def run_ours(args, spec) -> None:
             "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback 6.65 TB/s",
             "graph_replay_us_per_launch": graph_ms_per_step * 1e3,
             "graph_replay_achieved": per_step / (graph_ms_per_step * 1e-3) / 1e9,
+            "same_traffic_torch_op": same_traffic,
+            "frac_of_same_traffic_torch_op": achieved / same_traffic["achieved"],
         },
         "cpu_baseline": cpu,
         "e2e": e2e,
@@ -493,6 +497,42 @@ def run_ours(args, spec) -> None:
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
     dist.close()
+
+
+def copy_same_traffic(spec, rows: int, device, steps: int) -> dict:
+    """A torch elementwise op moving the same DRAM bytes as one step (add+RMSNorm: copy of the
+    x+residual bytes; SiLU: add of the gate and up halves into the output), timed the same way
+    (back-to-back over rotating buffers > 4x L2, CUDA events): the practical bandwidth at this
+    transfer size, beside the large-copy peak."""
+    import torch
+
+    if spec["op"] == "silu_and_mul":
+        read_elems, write_elems = 2 * rows * spec["intermediate"], rows * spec["intermediate"]
+    else:
+        read_elems = write_elems = 2 * rows * spec["hidden"]
+    per = 2 * (read_elems + write_elems)
+    sets = max(1, math.ceil(4 * L2_BYTES / per)) if per < 4 * L2_BYTES else 1
+    src = [torch.empty(read_elems, dtype=torch.bfloat16, device=device).normal_() for _ in range(sets)]
+    dst = [torch.empty(write_elems, dtype=torch.bfloat16, device=device) for _ in range(sets)]
+    if read_elems == write_elems:
+        def one(i: int) -> None:
+            dst[i % sets].copy_(src[i % sets])
+    else:
+        def one(i: int) -> None:
+            torch.add(src[i % sets][:write_elems], src[i % sets][write_elems:], out=dst[i % sets])
+    steps = max(3, min(steps, int(20e9 // per)))
+    for i in range(3):
+        one(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        one(i)
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) / steps * 1e3
+    return {"op": "torch copy" if read_elems == write_elems else "torch add", "us_per_launch": us,
+            "achieved": per / (us * 1e-6) / 1e9}
 
 
 def kernel_plan(spec, batches, rows: int) -> str:
@@ -578,10 +618,14 @@ def main() -> None:
     parser.add_argument("--e2e-steps", type=int, default=200)
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--rows", type=int, default=None,
+                        help="override the workload's row count (small cases for profiling)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
-    spec = WORKLOADS[args.workload]
+    spec = dict(WORKLOADS[args.workload])
+    if args.rows is not None:
+        spec["rows"] = args.rows
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world != args.gpus and "WORLD_SIZE" in os.environ:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)

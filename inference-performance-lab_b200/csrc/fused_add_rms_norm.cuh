@@ -50,21 +50,20 @@ struct StagedParams {
     int stage_bytes;    // bytes of one stage: x span then residual span
     int stages;         // ring depth S (any value >= 1; see the consumer's wait)
     int row_phase;      // element offset of row 0 of x (and residual) inside its 16-byte chunk
-    int shift_weight;   // 1: gamma's own phase differs from row_phase, build a shifted copy
     float epsilon;
 };
 
 // Shared memory map (dynamic):
 //   [stages * stage_bytes]      staged rows (x span, then residual span)
-//   [chunks_max * 16]           gamma as copied (16-byte aligned span around the weight)
-//   [chunks_max * 16]           gamma shifted to the rows' phase (only if shift_weight)
+//   [chunks_max * 16]           gamma as copied (bf16, 16-byte aligned span around the weight)
+//   [chunks_max * 32]           gamma widened to fp32 and aligned to the rows' phase
 //   [2 * stages + 1] mbarriers  S full, S empty, 1 gamma
 //   [2 * 16 floats]             cross-warp partial sums (two parities)
 //   [kStagedMaxStages ints]     per-stage count of warp releases (W per consumed row)
 //   [16 bytes]                  abort flag
 struct StagedLayout {
     uint32_t weight_raw_offset;
-    uint32_t weight_shifted_offset;
+    uint32_t weight_f32_offset;
     uint32_t barrier_offset;
     uint32_t reduce_offset;
     uint32_t released_offset;
@@ -72,13 +71,12 @@ struct StagedLayout {
     uint32_t total;
 };
 
-__host__ __device__ inline StagedLayout staged_layout(int stages, int stage_bytes, int chunks_max,
-                                                      int shift_weight) {
+__host__ __device__ inline StagedLayout staged_layout(int stages, int stage_bytes, int chunks_max) {
     StagedLayout l;
     const uint32_t span = static_cast<uint32_t>(chunks_max) * 16u;
     l.weight_raw_offset = static_cast<uint32_t>(stages) * static_cast<uint32_t>(stage_bytes);
-    l.weight_shifted_offset = l.weight_raw_offset + span;
-    l.barrier_offset = l.weight_shifted_offset + (shift_weight ? span : 0u);
+    l.weight_f32_offset = l.weight_raw_offset + span;
+    l.barrier_offset = l.weight_f32_offset + 2u * span;
     l.reduce_offset = l.barrier_offset + 8u * (2u * static_cast<uint32_t>(stages) + 1u);
     l.released_offset = l.reduce_offset + 2u * kStagedConsumerWarps * 4u;
     l.abort_offset = l.released_offset + 4u * kStagedMaxStages;
@@ -86,29 +84,36 @@ __host__ __device__ inline StagedLayout staged_layout(int stages, int stage_byte
     return l;
 }
 
-// Processes the 8 elements of one 16-byte chunk. `first` is the row column of element 0 of the
-// chunk (negative, or running past H, for the partial first and last chunks).
-template <bool kPass2>
-__device__ __forceinline__ void staged_chunk(const U32x4& xs, const U32x4& rs, const U32x4& ws,
-                                             int first, int hidden, float inv, float& sumsq,
-                                             U32x4& out, bool& full) {
-    full = first >= 0 && first + 8 <= hidden;
+// The 8 values of a staged chunk as four fp32 pairs (element 2i in the low half of pair i).
+struct Pairs4 {
+    F32x2 v[4];
+};
+
+__device__ __forceinline__ Pairs4 chunk_sum(const U32x4& xs, const U32x4& rs) {
+    Pairs4 v;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v.v[i] = f32x2_add(bf16x2_widen(xs.v[i]), bf16x2_widen(rs.v[i]));
+    return v;
+}
+
+// Zeroes the elements of a partial chunk that lie outside the row ([0, hidden)).
+__device__ __forceinline__ void mask_outside(Pairs4& v, int first, int hidden) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float v0 = __fadd_rn(bf16_lo(xs.v[i]), bf16_lo(rs.v[i]));
-        const float v1 = __fadd_rn(bf16_hi(xs.v[i]), bf16_hi(rs.v[i]));
-        if constexpr (!kPass2) {
-            const bool ok0 = full || (first + 2 * i >= 0 && first + 2 * i < hidden);
-            const bool ok1 = full || (first + 2 * i + 1 >= 0 && first + 2 * i + 1 < hidden);
-            sumsq = fmaf(ok0 ? v0 : 0.0f, ok0 ? v0 : 0.0f, sumsq);
-            sumsq = fmaf(ok1 ? v1 : 0.0f, ok1 ? v1 : 0.0f, sumsq);
-            out.v[i] = pack_bf16x2(v0, v1);
-        } else {
-            const float o0 = __fmul_rn(__fmul_rn(v0, inv), bf16_lo(ws.v[i]));
-            const float o1 = __fmul_rn(__fmul_rn(v1, inv), bf16_hi(ws.v[i]));
-            out.v[i] = pack_bf16x2(o0, o1);
-        }
+        float lo, hi;
+        f32x2_split(v.v[i], lo, hi);
+        const int c = first + 2 * i;
+        lo = (c >= 0 && c < hidden) ? lo : 0.0f;
+        hi = (c + 1 >= 0 && c + 1 < hidden) ? hi : 0.0f;
+        v.v[i] = f32x2_make(lo, hi);
     }
+}
+
+__device__ __forceinline__ U32x4 chunk_to_bf16(const Pairs4& v) {
+    U32x4 out;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) out.v[i] = f32x2_to_bf16x2(v.v[i]);
+    return out;
 }
 
 // Stores the valid elements of a chunk whose span is only partly inside the row.
@@ -133,20 +138,28 @@ __device__ __forceinline__ void store_chunk(uint16_t* chunk_base, const U32x4& o
     }
 }
 
-// Gamma for chunk k: 8 bf16 from shared memory. With shift 0 it is one aligned 16-byte load;
-// otherwise (rows whose phase differs from the staged gamma's, only when H % 8 != 0) it is
-// gathered element by element, zero outside the staged span.
-__device__ __forceinline__ U32x4 weight_chunk(uint32_t weight_base, int k, int shift, int span) {
-    if (shift == 0) return lds_v4(weight_base + 16u * k);
-    U32x4 ws;
+// fp32 gamma of chunk k as four pairs. With shift 0 two aligned 16-byte loads; otherwise (rows
+// whose phase differs from row 0's, only when H % 8 != 0) gathered element by element, zero
+// outside the staged span.
+__device__ __forceinline__ Pairs4 weight_chunk(uint32_t wf_base, int k, int shift, int span) {
+    Pairs4 w;
+    if (shift == 0) {
+        const U32x4 a = lds_v4(wf_base + 32u * k);
+        const U32x4 b = lds_v4(wf_base + 32u * k + 16u);
+        w.v[0] = f32x2_make(__uint_as_float(a.v[0]), __uint_as_float(a.v[1]));
+        w.v[1] = f32x2_make(__uint_as_float(a.v[2]), __uint_as_float(a.v[3]));
+        w.v[2] = f32x2_make(__uint_as_float(b.v[0]), __uint_as_float(b.v[1]));
+        w.v[3] = f32x2_make(__uint_as_float(b.v[2]), __uint_as_float(b.v[3]));
+        return w;
+    }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int i0 = 8 * k + 2 * i - shift;
-        const uint32_t lo = (i0 >= 0 && i0 < span) ? lds_u16(weight_base + 2u * i0) : 0u;
-        const uint32_t hi = (i0 + 1 >= 0 && i0 + 1 < span) ? lds_u16(weight_base + 2u * (i0 + 1)) : 0u;
-        ws.v[i] = lo | (hi << 16);
+        const float lo = (i0 >= 0 && i0 < span) ? lds_f32(wf_base + 4u * i0) : 0.0f;
+        const float hi = (i0 + 1 >= 0 && i0 + 1 < span) ? lds_f32(wf_base + 4u * (i0 + 1)) : 0.0f;
+        w.v[i] = f32x2_make(lo, hi);
     }
-    return ws;
+    return w;
 }
 
 template <int kWarpsPerRow>
@@ -157,7 +170,7 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
     constexpr int kConsumerThreads = kStagedConsumerWarps * kWarpSize;
 
     extern __shared__ __align__(128) unsigned char smem[];
-    const StagedLayout layout = staged_layout(p.stages, p.stage_bytes, p.chunks_max, p.shift_weight);
+    const StagedLayout layout = staged_layout(p.stages, p.stage_bytes, p.chunks_max);
     const uint32_t smem_base = smem_addr(smem);
     const uint32_t full_bar = smem_base + layout.barrier_offset;
     const uint32_t empty_bar = full_bar + 8u * static_cast<uint32_t>(p.stages);
@@ -234,23 +247,20 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
     // ---------------- consumers ----------------
     const int span = p.chunks_max * 8;
     if (!mbar_wait_bounded(weight_bar, 0, abort, kFaultFullBarrierTimeout)) return;
-    // Gamma index of row column c is c + gamma_phase in the staged copy.
-    int gamma_phase = weight_phase;
-    uint32_t weight_base = smem_base + layout.weight_raw_offset;
-    if (p.shift_weight) {
-        // Re-stage gamma with the rows' phase so that chunk k of a row lines up with bytes
-        // [16k, 16k + 16) of the copy.
+    // Widen gamma to fp32 once per CTA, aligned to row 0's phase: column c of a row whose
+    // phase is row_phase sits at index c + row_phase, so chunk k of such a row lines up with
+    // bytes [32k, 32k + 32) of the fp32 copy. Entries outside [0, H) are zero.
+    {
         const uint16_t* raw = reinterpret_cast<const uint16_t*>(smem + layout.weight_raw_offset);
-        uint16_t* shifted = reinterpret_cast<uint16_t*>(smem + layout.weight_shifted_offset);
+        float* wf = reinterpret_cast<float*>(smem + layout.weight_f32_offset);
         for (int i = threadIdx.x; i < span; i += kConsumerThreads) {
-            const int src = i - p.row_phase + weight_phase;
-            shifted[i] = (src >= 0 && src < span) ? raw[src] : static_cast<uint16_t>(0);
+            const int column = i - p.row_phase;
+            wf[i] = (column >= 0 && column < p.hidden) ? bf16_bits_to_float(raw[column + weight_phase]) : 0.0f;
         }
         named_barrier_sync(1, kConsumerThreads);
-        gamma_phase = p.row_phase;
-        weight_base = smem_base + layout.weight_shifted_offset;
     }
     grid_launch_dependents();
+    const uint32_t wf_base = smem_base + layout.weight_f32_offset;
 
     const int group = warp / kWarpsPerRow;
     const int warp_in_group = warp % kWarpsPerRow;
@@ -281,10 +291,10 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
         const int phase = static_cast<int>((xa & 15u) >> 1);
         const int chunks = (phase + p.hidden + 7) >> 3;
         const uint32_t stage = smem_base + static_cast<uint32_t>(s) * p.stage_bytes;
-        const int weight_shift = phase - gamma_phase;
+        const int weight_shift = phase - p.row_phase;
 
         // Pass 1: residual out + sum of squares (kStagedUnroll chunks loaded before use).
-        float sumsq = 0.0f;
+        F32x2 acc = f32x2_make(0.0f, 0.0f);
         for (int k0 = t; k0 < chunks; k0 += kGroupThreads * kStagedUnroll) {
             U32x4 xs[kStagedUnroll], rs[kStagedUnroll];
 #pragma unroll
@@ -299,14 +309,20 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
             for (int u = 0; u < kStagedUnroll; ++u) {
                 const int k = k0 + u * kGroupThreads;
                 if (k < chunks) {
-                    U32x4 out;
-                    bool full;
-                    staged_chunk<false>(xs[u], rs[u], xs[u], 8 * k - phase, p.hidden, 0.0f, sumsq, out, full);
-                    store_chunk(rbase + 8 * k, out, full, 8 * k - phase, p.hidden);
+                    const int first = 8 * k - phase;
+                    const bool full = first >= 0 && first + 8 <= p.hidden;
+                    Pairs4 v = chunk_sum(xs[u], rs[u]);
+                    const U32x4 out = chunk_to_bf16(v);
+                    if (!full) mask_outside(v, first, p.hidden);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) acc = f32x2_fma(v.v[i], v.v[i], acc);
+                    store_chunk(rbase + 8 * k, out, full, first, p.hidden);
                 }
             }
         }
-        sumsq = warp_sum(sumsq);
+        float acc_lo, acc_hi;
+        f32x2_split(acc, acc_lo, acc_hi);
+        float sumsq = warp_sum(acc_lo + acc_hi);
         if constexpr (kWarpsPerRow > 1) {
             float* slot = partials + parity_slot * kStagedConsumerWarps + group * kWarpsPerRow;
             if (lane == 0) slot[warp_in_group] = sumsq;
@@ -317,28 +333,31 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
             parity_slot ^= 1;
         }
         const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
+        const F32x2 inv2 = f32x2_make(inv, inv);
 
-        // Pass 2: normalised output, v recomputed from the staged bytes.
+        // Pass 2: normalised output (v * inv) * gamma, v recomputed from the staged bytes.
         for (int k0 = t; k0 < chunks; k0 += kGroupThreads * kStagedUnroll) {
-            U32x4 xs[kStagedUnroll], rs[kStagedUnroll], ws[kStagedUnroll];
+            U32x4 xs[kStagedUnroll], rs[kStagedUnroll];
+            Pairs4 ws[kStagedUnroll];
 #pragma unroll
             for (int u = 0; u < kStagedUnroll; ++u) {
                 const int k = k0 + u * kGroupThreads;
                 if (k < chunks) {
                     xs[u] = lds_v4(stage + 16u * k);
                     rs[u] = lds_v4(stage + half + 16u * k);
-                    ws[u] = weight_chunk(weight_base, k, weight_shift, span);
+                    ws[u] = weight_chunk(wf_base, k, weight_shift, span);
                 }
             }
 #pragma unroll
             for (int u = 0; u < kStagedUnroll; ++u) {
                 const int k = k0 + u * kGroupThreads;
                 if (k < chunks) {
-                    U32x4 out;
-                    bool full;
-                    float unused = 0.0f;
-                    staged_chunk<true>(xs[u], rs[u], ws[u], 8 * k - phase, p.hidden, inv, unused, out, full);
-                    store_chunk(xbase + 8 * k, out, full, 8 * k - phase, p.hidden);
+                    const int first = 8 * k - phase;
+                    const bool full = first >= 0 && first + 8 <= p.hidden;
+                    Pairs4 v = chunk_sum(xs[u], rs[u]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) v.v[i] = f32x2_mul(f32x2_mul(v.v[i], inv2), ws[u].v[i]);
+                    store_chunk(xbase + 8 * k, chunk_to_bf16(v), full, first, p.hidden);
                 }
             }
         }

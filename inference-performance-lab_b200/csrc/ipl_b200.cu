@@ -131,19 +131,16 @@ ipl_status check_rms_args(const void* x, const void* residual, const void* weigh
 }
 
 // Pure function of the arguments and two device limits.
-RmsPlan plan_rms(const void* x, const void* residual, const void* weight, int64_t rows, int64_t hidden,
-                 int sm_count, int smem_limit) {
+RmsPlan plan_rms(const void* x, const void* residual, int64_t rows, int64_t hidden, int sm_count,
+                 int smem_limit) {
     RmsPlan plan;
     if (rows == 0) return plan;
     const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
     const uintptr_t ra = reinterpret_cast<uintptr_t>(residual);
-    const uintptr_t wa = reinterpret_cast<uintptr_t>(weight);
     const int chunks_max = static_cast<int>((hidden + 7) / 8 + 1);
     const int stage_bytes = 2 * chunks_max * 16;
     const int row_phase = static_cast<int>((xa & 15u) >> 1);
-    // Gamma needs a shifted copy when every row has one phase (H % 8 == 0) and gamma's differs.
-    const int shift_weight = (hidden % 8 == 0 && row_phase != static_cast<int>((wa & 15u) >> 1)) ? 1 : 0;
-    const StagedLayout fixed = staged_layout(0, stage_bytes, chunks_max, shift_weight);
+    const StagedLayout fixed = staged_layout(0, stage_bytes, chunks_max);
     const int64_t room = static_cast<int64_t>(smem_limit) - fixed.total;
     int max_stages = room > 0 ? static_cast<int>(room / (stage_bytes + 2 * 8)) : 0;
     if (max_stages > kStagedMaxStages) max_stages = kStagedMaxStages;
@@ -191,8 +188,7 @@ RmsPlan plan_rms(const void* x, const void* residual, const void* weight, int64_
         plan.staged.stage_bytes = stage_bytes;
         plan.staged.stages = stages;
         plan.staged.row_phase = row_phase;
-        plan.staged.shift_weight = shift_weight;
-        plan.smem = staged_layout(stages, stage_bytes, chunks_max, shift_weight).total;
+        plan.smem = staged_layout(stages, stage_bytes, chunks_max).total;
         return plan;
     }
     plan.kernel = hidden <= static_cast<int64_t>(kRowwiseThreads) * kRowwiseCachedPerThread
@@ -348,7 +344,7 @@ ipl_status ipl_fused_add_rms_norm_bf16(void* x, void* residual, const void* weig
     DeviceInfo* info = nullptr;
     st = current_device(&device, &info);
     if (st != IPL_SUCCESS) return st;
-    RmsPlan plan = plan_rms(x, residual, weight, rows, hidden_size,
+    RmsPlan plan = plan_rms(x, residual, rows, hidden_size,
                             info->sm_count.load(std::memory_order_relaxed),
                             info->max_smem_optin.load(std::memory_order_relaxed));
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
@@ -441,7 +437,7 @@ const char* ipl_fused_add_rms_norm_plan(const void* x, const void* residual, con
                                         int64_t hidden_size) {
     if (check_rms_args(x, residual, weight, rows, hidden_size, 1.0) != IPL_SUCCESS) return "invalid";
     // B200 limits: 148 SMs, 232448 bytes of opt-in shared memory per block.
-    return rms_kernel_name(plan_rms(x, residual, weight, rows, hidden_size, 148, 232448).kernel);
+    return rms_kernel_name(plan_rms(x, residual, rows, hidden_size, 148, 232448).kernel);
 }
 
 const char* ipl_silu_and_mul_plan(const void* output, const void* input, int64_t rows,

@@ -43,6 +43,44 @@ __device__ __forceinline__ uint16_t float_to_bf16_bits(float value) {
     return static_cast<uint16_t>(pack_bf16x2(value, 0.0f) & 0xffffu);
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two IEEE fp32 ops) ------
+
+using F32x2 = unsigned long long;  // .b64 register pair: low half = first float
+
+__device__ __forceinline__ F32x2 f32x2_make(float lo, float hi) {
+    F32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f32x2_split(F32x2 v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ F32x2 f32x2_add(F32x2 a, F32x2 b) {
+    F32x2 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ F32x2 f32x2_mul(F32x2 a, F32x2 b) {
+    F32x2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ F32x2 f32x2_fma(F32x2 a, F32x2 b, F32x2 c) {
+    F32x2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+// bf16x2 word -> fp32 pair (exact).
+__device__ __forceinline__ F32x2 bf16x2_widen(uint32_t packed) {
+    return f32x2_make(__uint_as_float(packed << 16), __uint_as_float(packed & 0xffff0000u));
+}
+// fp32 pair -> bf16x2 word, round to nearest even.
+__device__ __forceinline__ uint32_t f32x2_to_bf16x2(F32x2 v) {
+    float lo, hi;
+    f32x2_split(v, lo, hi);
+    return pack_bf16x2(lo, hi);
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -96,6 +134,11 @@ __device__ __forceinline__ U32x4 lds_v4(uint32_t addr) {
     asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3])
                  : "r"(addr));
+    return r;
+}
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+    float r;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"(addr));
     return r;
 }
 __device__ __forceinline__ uint16_t lds_u16(uint32_t addr) {

@@ -45,9 +45,11 @@ __device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv32& f) {
 }
 
 __device__ __forceinline__ float silu_mul(float gate, float up) {
-    // gate * (1 / (1 + e^-gate)): e^-gate overflows to +inf for gate < -88, giving 0 * gate.
-    const float sig = __frcp_rn(__fadd_rn(1.0f, __expf(-gate)));
-    return __fmul_rn(__fmul_rn(gate, sig), up);
+    // gate / (1 + e^-gate) with the hardware exponential and fast division (a few ulp in fp32,
+    // far below the bf16 rounding of the result). For gate < -87.3 the denominator exceeds
+    // 2^126 and the quotient is 0 (the exact value is below 1e-36); gate = -inf gives NaN and
+    // gate = +inf gives +inf, as in the reference.
+    return __fmul_rn(__fdividef(gate, __fadd_rn(1.0f, __expf(-gate))), up);
 }
 
 template <int kWords>
