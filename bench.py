@@ -608,7 +608,18 @@ def run_e2e(args, spec, rows: int, batches, weight, stream, dist) -> dict:
     }
 
 
+def _reserve_stdout_for_the_result() -> None:
+    """Only the result line goes to stdout: libraries that print from C (NCCL's version banner,
+    for one) are sent to stderr by pointing file descriptor 1 there, and Python's stdout is
+    re-opened on a private duplicate of the original descriptor."""
+    sys.stdout.flush()
+    result_fd = os.dup(1)
+    os.dup2(2, 1)
+    sys.stdout = os.fdopen(result_fd, "w", buffering=1)
+
+
 def main() -> None:
+    _reserve_stdout_for_the_result()
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=3000)

@@ -59,6 +59,23 @@ IPL_API ipl_status ipl_fused_add_rms_norm_bf16(void* x, void* residual, const vo
                                        int64_t hidden_size, double epsilon, void* stream);
 
 /*
+ * RMSNorm without a residual, out of place (output may equal input):
+ *
+ *   output = bf16((fp32(input) * rsqrt(mean(fp32(input)^2) + epsilon)) * fp32(weight))
+ *
+ * input, output: [rows, hidden_size] contiguous; weight: [hidden_size]. Any alignment is
+ * accepted (output sharing input's offset modulo 16 bytes takes the staged kernel).
+ *
+ * No counterpart in the reference's C++ sources: it is the plain rms_norm of the vLLM IR that
+ * the reference's plugin targets (vllm/ir/ops/layernorm.py:9-21 of vLLM 0.22, the op before the
+ * first and after the last decoder layer), with vLLM's torch.ops._C.rms_norm(out, input, weight,
+ * epsilon) argument order and the reference oracle's fp32 arithmetic
+ * (src/inference_performance_lab/kernels/reference.py:18-23 with a zero residual).
+ */
+IPL_API ipl_status ipl_rms_norm_bf16(void* output, const void* input, const void* weight, int64_t rows,
+                                     int64_t hidden_size, double epsilon, void* stream);
+
+/*
  * SiLU-and-multiply: output[r, c] = bf16(silu(fp32(input[r, c])) * fp32(input[r, I + c])),
  * I = intermediate_size, input [rows, 2*I] and output [rows, I], both contiguous. Any width and
  * alignment is accepted; aligned widths take the vector path. rows * I == 0 is a no-op.
@@ -104,12 +121,15 @@ IPL_API ipl_status ipl_device_fault_flags(int device, uint32_t* flags);
 IPL_API ipl_status ipl_clear_device_fault_flags(int device);
 
 /*
- * Name of the kernel that ipl_fused_add_rms_norm_bf16 / ipl_silu_and_mul_bf16 would launch for
+ * Name of the kernel that ipl_fused_add_rms_norm_bf16 / ipl_rms_norm_bf16 / ipl_silu_and_mul_bf16
+ * would launch for
  * these arguments (no launch, no device access). Static string; "none" for an empty batch,
  * "invalid" when the arguments would be rejected.
  */
 IPL_API const char* ipl_fused_add_rms_norm_plan(const void* x, const void* residual, const void* weight,
                                         int64_t rows, int64_t hidden_size);
+IPL_API const char* ipl_rms_norm_plan(const void* output, const void* input, const void* weight,
+                                      int64_t rows, int64_t hidden_size);
 IPL_API const char* ipl_silu_and_mul_plan(const void* output, const void* input, int64_t rows,
                                   int64_t intermediate_size);
 

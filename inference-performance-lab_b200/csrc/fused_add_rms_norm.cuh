@@ -41,13 +41,14 @@ constexpr int kRowwiseThreads = 256;
 constexpr int kRowwiseCachedPerThread = 16;  // rows up to 4096 elements keep v in registers
 
 struct StagedParams {
-    uint16_t* x;
-    uint16_t* residual;
+    uint16_t* x;          // input rows (and the normalised output of the fused op)
+    uint16_t* residual;   // fused op: residual rows, updated in place; plain RMSNorm: unused
+    uint16_t* out;        // normalised output rows (== x for the fused op)
     const uint16_t* weight;
     int64_t rows;
     int hidden;
     int chunks_max;     // 16-byte chunks in one staged row (covers any phase)
-    int stage_bytes;    // bytes of one stage: x span then residual span
+    int stage_bytes;    // bytes of one stage: x span, then (fused op) residual span
     int stages;         // ring depth S (any value >= 1; see the consumer's wait)
     int row_phase;      // element offset of row 0 of x (and residual) inside its 16-byte chunk
     float epsilon;
@@ -56,7 +57,10 @@ struct StagedParams {
 // Shared memory map (dynamic):
 //   [stages * stage_bytes]      staged rows (x span, then residual span)
 //   [chunks_max * 16]           gamma as copied (bf16, 16-byte aligned span around the weight)
-//   [chunks_max * 32]           gamma widened to fp32 and aligned to the rows' phase
+//   [chunks_max * 32]           gamma widened to fp32 and aligned to the rows' phase, in two
+//                               planes of chunks_max * 16 bytes: elements 0-3 of chunk k at
+//                               plane 0 + 16k, elements 4-7 at plane 1 + 16k (a warp's 16-byte
+//                               loads of consecutive chunks then hit consecutive banks)
 //   [2 * stages + 1] mbarriers  S full, S empty, 1 gamma
 //   [2 * 16 floats]             cross-warp partial sums (two parities)
 //   [kStagedMaxStages ints]     per-stage count of warp releases (W per consumed row)
@@ -93,6 +97,13 @@ __device__ __forceinline__ Pairs4 chunk_sum(const U32x4& xs, const U32x4& rs) {
     Pairs4 v;
 #pragma unroll
     for (int i = 0; i < 4; ++i) v.v[i] = f32x2_add(bf16x2_widen(xs.v[i]), bf16x2_widen(rs.v[i]));
+    return v;
+}
+
+__device__ __forceinline__ Pairs4 chunk_widen(const U32x4& xs) {
+    Pairs4 v;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v.v[i] = bf16x2_widen(xs.v[i]);
     return v;
 }
 
@@ -138,31 +149,36 @@ __device__ __forceinline__ void store_chunk(uint16_t* chunk_base, const U32x4& o
     }
 }
 
-// fp32 gamma of chunk k as four pairs. With shift 0 two aligned 16-byte loads; otherwise (rows
-// whose phase differs from row 0's, only when H % 8 != 0) gathered element by element, zero
-// outside the staged span.
-__device__ __forceinline__ Pairs4 weight_chunk(uint32_t wf_base, int k, int shift, int span) {
+// Byte offset of fp32 gamma element i (element i % 8 of chunk i / 8) in the two-plane layout.
+__device__ __forceinline__ uint32_t gamma_offset(int i, uint32_t plane_bytes) {
+    return 16u * static_cast<uint32_t>(i >> 3) + ((i & 4) ? plane_bytes : 0u) + 4u * static_cast<uint32_t>(i & 3);
+}
+
+// fp32 gamma of chunk k as four pairs. With shift 0 two 16-byte loads (one per plane); otherwise
+// (rows whose phase differs from row 0's, only when H % 8 != 0) gathered element by element,
+// zero outside the staged span.
+__device__ __forceinline__ Pairs4 weight_chunk(uint32_t wf_base, uint32_t plane_bytes, int k, int shift,
+                                               int span) {
     Pairs4 w;
     if (shift == 0) {
-        const U32x4 a = lds_v4(wf_base + 32u * k);
-        const U32x4 b = lds_v4(wf_base + 32u * k + 16u);
-        w.v[0] = f32x2_make(__uint_as_float(a.v[0]), __uint_as_float(a.v[1]));
-        w.v[1] = f32x2_make(__uint_as_float(a.v[2]), __uint_as_float(a.v[3]));
-        w.v[2] = f32x2_make(__uint_as_float(b.v[0]), __uint_as_float(b.v[1]));
-        w.v[3] = f32x2_make(__uint_as_float(b.v[2]), __uint_as_float(b.v[3]));
+        lds_pairs(wf_base + 16u * k, w.v[0], w.v[1]);
+        lds_pairs(wf_base + plane_bytes + 16u * k, w.v[2], w.v[3]);
         return w;
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int i0 = 8 * k + 2 * i - shift;
-        const float lo = (i0 >= 0 && i0 < span) ? lds_f32(wf_base + 4u * i0) : 0.0f;
-        const float hi = (i0 + 1 >= 0 && i0 + 1 < span) ? lds_f32(wf_base + 4u * (i0 + 1)) : 0.0f;
+        const float lo = (i0 >= 0 && i0 < span) ? lds_f32(wf_base + gamma_offset(i0, plane_bytes)) : 0.0f;
+        const float hi =
+            (i0 + 1 >= 0 && i0 + 1 < span) ? lds_f32(wf_base + gamma_offset(i0 + 1, plane_bytes)) : 0.0f;
         w.v[i] = f32x2_make(lo, hi);
     }
     return w;
 }
 
-template <int kWarpsPerRow>
+// kResidual: the fused residual add (x, residual -> residual = bf16(x + r), x = norm) when
+// true; plain RMSNorm (x -> out = norm(x)) when false. out must share x's offset modulo 16.
+template <int kWarpsPerRow, bool kResidual>
 __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const StagedParams p) {
     static_assert(kStagedConsumerWarps % kWarpsPerRow == 0, "groups must tile the consumer warps");
     constexpr int kGroups = kStagedConsumerWarps / kWarpsPerRow;
@@ -228,7 +244,7 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
                 }
                 const int64_t row = row_begin + j;
                 const uintptr_t xa = reinterpret_cast<uintptr_t>(p.x + row * p.hidden);
-                const uintptr_t ra = reinterpret_cast<uintptr_t>(p.residual + row * p.hidden);
+                const uintptr_t ra = kResidual ? reinterpret_cast<uintptr_t>(p.residual + row * p.hidden) : 0;
                 const uintptr_t xbase = xa & ~static_cast<uintptr_t>(15);
                 const uintptr_t rbase = ra & ~static_cast<uintptr_t>(15);
                 const uint32_t phase = static_cast<uint32_t>(xa - xbase) >> 1;
@@ -236,9 +252,11 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
                 const uint32_t bytes = chunks * 16u;
                 const uint32_t stage = smem_base + static_cast<uint32_t>(s) * p.stage_bytes;
                 const uint32_t bar = full_bar + 8u * static_cast<uint32_t>(s);
-                mbar_arrive_expect_tx(bar, 2u * bytes);
+                mbar_arrive_expect_tx(bar, kResidual ? 2u * bytes : bytes);
                 bulk_load(stage, reinterpret_cast<const void*>(xbase), bytes, bar, policy);
-                bulk_load(stage + half, reinterpret_cast<const void*>(rbase), bytes, bar, policy);
+                if constexpr (kResidual) {
+                    bulk_load(stage + half, reinterpret_cast<const void*>(rbase), bytes, bar, policy);
+                }
             }
         }
         return;
@@ -252,10 +270,11 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
     // bytes [32k, 32k + 32) of the fp32 copy. Entries outside [0, H) are zero.
     {
         const uint16_t* raw = reinterpret_cast<const uint16_t*>(smem + layout.weight_raw_offset);
-        float* wf = reinterpret_cast<float*>(smem + layout.weight_f32_offset);
+        unsigned char* wf = smem + layout.weight_f32_offset;
         for (int i = threadIdx.x; i < span; i += kConsumerThreads) {
             const int column = i - p.row_phase;
-            wf[i] = (column >= 0 && column < p.hidden) ? bf16_bits_to_float(raw[column + weight_phase]) : 0.0f;
+            *reinterpret_cast<float*>(wf + gamma_offset(i, half)) =
+                (column >= 0 && column < p.hidden) ? bf16_bits_to_float(raw[column + weight_phase]) : 0.0f;
         }
         named_barrier_sync(1, kConsumerThreads);
     }
@@ -266,6 +285,12 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
     const int warp_in_group = warp % kWarpsPerRow;
     const int t = threadIdx.x % kGroupThreads;
     const float hidden_f = static_cast<float>(p.hidden);
+
+    // When every row of this CTA has a stage of its own, no bulk copy ever refills a stage, so
+    // pass 1 may overwrite the staged bytes with v (fp32) for pass 2 to read back. A refilled stage
+    // would need a generic-to-async proxy fence before its release; streaming CTAs recompute v
+    // from the staged x and residual instead.
+    const bool stash = kResidual && local_rows <= p.stages;
 
     int parity_slot = 0;
     for (int j = group; j < local_rows; j += kGroups) {
@@ -285,15 +310,20 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
         if (!mbar_wait_bounded(bar, round & 1, abort, kFaultFullBarrierTimeout)) break;
         const int64_t row = row_begin + j;
         const uintptr_t xa = reinterpret_cast<uintptr_t>(p.x + row * p.hidden);
-        const uintptr_t ra = reinterpret_cast<uintptr_t>(p.residual + row * p.hidden);
-        uint16_t* xbase = reinterpret_cast<uint16_t*>(xa & ~static_cast<uintptr_t>(15));
+        const uintptr_t ra = kResidual ? reinterpret_cast<uintptr_t>(p.residual + row * p.hidden) : 0;
+        const uintptr_t oa = reinterpret_cast<uintptr_t>(p.out + row * p.hidden);
+        uint16_t* obase = reinterpret_cast<uint16_t*>(oa & ~static_cast<uintptr_t>(15));
         uint16_t* rbase = reinterpret_cast<uint16_t*>(ra & ~static_cast<uintptr_t>(15));
         const int phase = static_cast<int>((xa & 15u) >> 1);
         const int chunks = (phase + p.hidden + 7) >> 3;
         const uint32_t stage = smem_base + static_cast<uint32_t>(s) * p.stage_bytes;
         const int weight_shift = phase - p.row_phase;
 
-        // Pass 1: residual out + sum of squares (kStagedUnroll chunks loaded before use).
+        // Pass 1: residual out + sum of squares (kStagedUnroll chunks loaded before use). With
+        // `stash`, the fp32 sum v of chunk k replaces the chunk's staged bytes in place (elements
+        // 0-3 over the x chunk, 4-7 over the residual chunk: 16 + 16 bytes either way), so pass 2
+        // reads v back instead of widening and adding again; each thread rewrites only the
+        // chunks it read.
         F32x2 acc = f32x2_make(0.0f, 0.0f);
         for (int k0 = t; k0 < chunks; k0 += kGroupThreads * kStagedUnroll) {
             U32x4 xs[kStagedUnroll], rs[kStagedUnroll];
@@ -302,7 +332,7 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
                 const int k = k0 + u * kGroupThreads;
                 if (k < chunks) {
                     xs[u] = lds_v4(stage + 16u * k);
-                    rs[u] = lds_v4(stage + half + 16u * k);
+                    if constexpr (kResidual) rs[u] = lds_v4(stage + half + 16u * k);
                 }
             }
 #pragma unroll
@@ -311,12 +341,21 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
                 if (k < chunks) {
                     const int first = 8 * k - phase;
                     const bool full = first >= 0 && first + 8 <= p.hidden;
-                    Pairs4 v = chunk_sum(xs[u], rs[u]);
-                    const U32x4 out = chunk_to_bf16(v);
+                    Pairs4 v;
+                    if constexpr (kResidual) {
+                        v = chunk_sum(xs[u], rs[u]);
+                        const U32x4 out = chunk_to_bf16(v);
+                        if (stash) {
+                            sts_pairs(stage + 16u * k, v.v[0], v.v[1]);
+                            sts_pairs(stage + half + 16u * k, v.v[2], v.v[3]);
+                        }
+                        store_chunk(rbase + 8 * k, out, full, first, p.hidden);
+                    } else {
+                        v = chunk_widen(xs[u]);
+                    }
                     if (!full) mask_outside(v, first, p.hidden);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) acc = f32x2_fma(v.v[i], v.v[i], acc);
-                    store_chunk(rbase + 8 * k, out, full, first, p.hidden);
                 }
             }
         }
@@ -335,17 +374,22 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
         const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
         const F32x2 inv2 = f32x2_make(inv, inv);
 
-        // Pass 2: normalised output (v * inv) * gamma, v recomputed from the staged bytes.
+        // Pass 2: normalised output (v * inv) * gamma; v read back (stash) or recomputed.
         for (int k0 = t; k0 < chunks; k0 += kGroupThreads * kStagedUnroll) {
-            U32x4 xs[kStagedUnroll], rs[kStagedUnroll];
-            Pairs4 ws[kStagedUnroll];
+            Pairs4 vs[kStagedUnroll], ws[kStagedUnroll];
 #pragma unroll
             for (int u = 0; u < kStagedUnroll; ++u) {
                 const int k = k0 + u * kGroupThreads;
                 if (k < chunks) {
-                    xs[u] = lds_v4(stage + 16u * k);
-                    rs[u] = lds_v4(stage + half + 16u * k);
-                    ws[u] = weight_chunk(wf_base, k, weight_shift, span);
+                    if (stash) {
+                        lds_pairs(stage + 16u * k, vs[u].v[0], vs[u].v[1]);
+                        lds_pairs(stage + half + 16u * k, vs[u].v[2], vs[u].v[3]);
+                    } else if constexpr (kResidual) {
+                        vs[u] = chunk_sum(lds_v4(stage + 16u * k), lds_v4(stage + half + 16u * k));
+                    } else {
+                        vs[u] = chunk_widen(lds_v4(stage + 16u * k));
+                    }
+                    ws[u] = weight_chunk(wf_base, half, k, weight_shift, span);
                 }
             }
 #pragma unroll
@@ -354,10 +398,10 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
                 if (k < chunks) {
                     const int first = 8 * k - phase;
                     const bool full = first >= 0 && first + 8 <= p.hidden;
-                    Pairs4 v = chunk_sum(xs[u], rs[u]);
+                    Pairs4 v;
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) v.v[i] = f32x2_mul(f32x2_mul(v.v[i], inv2), ws[u].v[i]);
-                    store_chunk(xbase + 8 * k, chunk_to_bf16(v), full, first, p.hidden);
+                    for (int i = 0; i < 4; ++i) v.v[i] = f32x2_mul(f32x2_mul(vs[u].v[i], inv2), ws[u].v[i]);
+                    store_chunk(obase + 8 * k, chunk_to_bf16(v), full, first, p.hidden);
                 }
             }
         }
@@ -386,18 +430,27 @@ __device__ __forceinline__ float block_sum_rowwise(float value, float* partials)
 }
 
 // kCached: v kept in registers (H <= kRowwiseThreads * kRowwiseCachedPerThread); otherwise the
-// row is read twice.
-template <bool kCached>
+// row is read twice. kResidual as for the staged kernel; out may alias x.
+template <bool kCached, bool kResidual>
 __global__ void __launch_bounds__(kRowwiseThreads) rmsnorm_rowwise_kernel(
-    uint16_t* __restrict__ x, uint16_t* __restrict__ residual, const uint16_t* __restrict__ weight,
-    int64_t rows, int hidden, float epsilon) {
+    const uint16_t* x, uint16_t* residual, uint16_t* out, const uint16_t* __restrict__ weight, int64_t rows,
+    int hidden, float epsilon) {
     __shared__ float partials[kRowwiseThreads / kWarpSize];
     grid_dependency_wait();
     grid_launch_dependents();
     const float den = static_cast<float>(hidden);
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-        uint16_t* xr = x + row * hidden;
-        uint16_t* rr = residual + row * hidden;
+        const uint16_t* xr = x + row * hidden;
+        uint16_t* rr = kResidual ? residual + row * hidden : nullptr;
+        uint16_t* orow = out + row * hidden;
+        auto load_v = [&](int c) {
+            const float xv = bf16_bits_to_float(xr[c]);
+            if constexpr (kResidual) {
+                return __fadd_rn(xv, bf16_bits_to_float(rr[c]));
+            } else {
+                return xv;
+            }
+        };
         float sumsq = 0.0f;
         float cache[kCached ? kRowwiseCachedPerThread : 1];
         if constexpr (kCached) {
@@ -406,16 +459,16 @@ __global__ void __launch_bounds__(kRowwiseThreads) rmsnorm_rowwise_kernel(
                 const int c = threadIdx.x + i * kRowwiseThreads;
                 cache[i] = 0.0f;
                 if (c < hidden) {
-                    const float v = __fadd_rn(bf16_bits_to_float(xr[c]), bf16_bits_to_float(rr[c]));
+                    const float v = load_v(c);
                     cache[i] = v;
-                    sumsq += __fmul_rn(v, v);
-                    rr[c] = float_to_bf16_bits(v);
+                    sumsq = fmaf(v, v, sumsq);
+                    if constexpr (kResidual) rr[c] = float_to_bf16_bits(v);
                 }
             }
         } else {
             for (int c = threadIdx.x; c < hidden; c += kRowwiseThreads) {
-                const float v = __fadd_rn(bf16_bits_to_float(xr[c]), bf16_bits_to_float(rr[c]));
-                sumsq += __fmul_rn(v, v);
+                const float v = load_v(c);
+                sumsq = fmaf(v, v, sumsq);
             }
         }
         sumsq = block_sum_rowwise(sumsq, partials);
@@ -425,15 +478,15 @@ __global__ void __launch_bounds__(kRowwiseThreads) rmsnorm_rowwise_kernel(
             for (int i = 0; i < kRowwiseCachedPerThread; ++i) {
                 const int c = threadIdx.x + i * kRowwiseThreads;
                 if (c < hidden) {
-                    xr[c] = float_to_bf16_bits(
+                    orow[c] = float_to_bf16_bits(
                         __fmul_rn(__fmul_rn(cache[i], inv), bf16_bits_to_float(weight[c])));
                 }
             }
         } else {
             for (int c = threadIdx.x; c < hidden; c += kRowwiseThreads) {
-                const float v = __fadd_rn(bf16_bits_to_float(xr[c]), bf16_bits_to_float(rr[c]));
-                rr[c] = float_to_bf16_bits(v);
-                xr[c] = float_to_bf16_bits(__fmul_rn(__fmul_rn(v, inv), bf16_bits_to_float(weight[c])));
+                const float v = load_v(c);
+                if constexpr (kResidual) rr[c] = float_to_bf16_bits(v);
+                orow[c] = float_to_bf16_bits(__fmul_rn(__fmul_rn(v, inv), bf16_bits_to_float(weight[c])));
             }
         }
     }

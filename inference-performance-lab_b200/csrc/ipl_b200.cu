@@ -79,73 +79,78 @@ cudaError_t launch(Kernel kernel, unsigned grid, unsigned block, size_t smem, cu
 }
 
 // ------------------------------------------------------------------------------------------
-// add + RMSNorm planning
+// add + RMSNorm / RMSNorm planning
 
-enum class RmsKernel {
-    kNone,
-    kStaged1,
-    kStaged2,
-    kStaged4,
-    kStaged8,
-    kStaged16,
-    kRowwiseCached,
-    kRowwiseTwoPass
-};
-
-const char* rms_kernel_name(RmsKernel k) {
-    switch (k) {
-        case RmsKernel::kNone: return "none";
-        case RmsKernel::kStaged1: return "rmsnorm_staged_kernel<1>";
-        case RmsKernel::kStaged2: return "rmsnorm_staged_kernel<2>";
-        case RmsKernel::kStaged4: return "rmsnorm_staged_kernel<4>";
-        case RmsKernel::kStaged8: return "rmsnorm_staged_kernel<8>";
-        case RmsKernel::kStaged16: return "rmsnorm_staged_kernel<16>";
-        case RmsKernel::kRowwiseCached: return "rmsnorm_rowwise_kernel<cached>";
-        case RmsKernel::kRowwiseTwoPass: return "rmsnorm_rowwise_kernel<two-pass>";
-    }
-    return "invalid";
-}
+enum class RmsFamily { kNone, kStaged, kRowwiseCached, kRowwiseTwoPass };
 
 struct RmsPlan {
-    RmsKernel kernel = RmsKernel::kNone;
+    RmsFamily family = RmsFamily::kNone;
+    int warps_per_row = 0;  // staged kernels: 1, 2, 4, 8 or 16
     unsigned grid = 0;
     size_t smem = 0;
     StagedParams staged = {};
 };
 
-ipl_status check_rms_args(const void* x, const void* residual, const void* weight, int64_t rows,
-                          int64_t hidden, double epsilon) {
+// Kernel names as reported by the plan queries (static strings).
+const char* rms_kernel_name(const RmsPlan& plan, bool residual) {
+    static const char* const kStagedNames[2][5] = {
+        {"rmsnorm_staged_kernel<1, plain>", "rmsnorm_staged_kernel<2, plain>", "rmsnorm_staged_kernel<4, plain>",
+         "rmsnorm_staged_kernel<8, plain>", "rmsnorm_staged_kernel<16, plain>"},
+        {"rmsnorm_staged_kernel<1>", "rmsnorm_staged_kernel<2>", "rmsnorm_staged_kernel<4>",
+         "rmsnorm_staged_kernel<8>", "rmsnorm_staged_kernel<16>"}};
+    switch (plan.family) {
+        case RmsFamily::kNone: return "none";
+        case RmsFamily::kStaged: {
+            int i = 0;
+            while ((1 << i) < plan.warps_per_row) ++i;
+            return kStagedNames[residual ? 1 : 0][i];
+        }
+        case RmsFamily::kRowwiseCached:
+            return residual ? "rmsnorm_rowwise_kernel<cached>" : "rmsnorm_rowwise_kernel<cached, plain>";
+        case RmsFamily::kRowwiseTwoPass:
+            return residual ? "rmsnorm_rowwise_kernel<two-pass>" : "rmsnorm_rowwise_kernel<two-pass, plain>";
+    }
+    return "invalid";
+}
+
+// x, weight and (fused op) residual / (plain op) out: the three row pointers of a call.
+ipl_status check_rms_args(const void* x, const void* other, const void* weight, int64_t rows, int64_t hidden,
+                          double epsilon, bool residual) {
     if (rows < 0) return fail(IPL_ERROR_INVALID_VALUE, "number of rows must be non-negative");
     if (hidden <= 0) return fail(IPL_ERROR_INVALID_VALUE, "x must have a non-empty final dimension");
     if (!(epsilon > 0.0)) return fail(IPL_ERROR_INVALID_VALUE, "epsilon must be positive");
     if (hidden > INT_MAX) return fail(IPL_ERROR_TOO_LARGE, "hidden dimension is too large");
     if (rows > INT_MAX) return fail(IPL_ERROR_TOO_LARGE, "number of rows is too large");
-    if (rows > 0 && (x == nullptr || residual == nullptr || weight == nullptr)) {
-        return fail(IPL_ERROR_INVALID_VALUE, "x, residual and weight must be non-null");
+    if (rows > 0 && (x == nullptr || other == nullptr || weight == nullptr)) {
+        return fail(IPL_ERROR_INVALID_VALUE, residual ? "x, residual and weight must be non-null"
+                                                      : "output, input and weight must be non-null");
     }
-    const uintptr_t odd = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(residual) |
+    const uintptr_t odd = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(other) |
                           reinterpret_cast<uintptr_t>(weight);
     if (odd & 1u) return fail(IPL_ERROR_INVALID_VALUE, "bfloat16 pointers must be 2-byte aligned");
-    if (rows > 0 && x == residual) return fail(IPL_ERROR_INVALID_VALUE, "x and residual must not alias");
+    if (residual && rows > 0 && x == other) {
+        return fail(IPL_ERROR_INVALID_VALUE, "x and residual must not alias");
+    }
     return IPL_SUCCESS;
 }
 
-// Pure function of the arguments and two device limits.
-RmsPlan plan_rms(const void* x, const void* residual, int64_t rows, int64_t hidden, int sm_count,
+// Pure function of the arguments and two device limits. `other` is the residual (fused op) or
+// the output (plain op); either must share x's offset modulo 16 bytes for the staged kernel.
+RmsPlan plan_rms(const void* x, const void* other, int64_t rows, int64_t hidden, bool residual, int sm_count,
                  int smem_limit) {
     RmsPlan plan;
     if (rows == 0) return plan;
     const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
-    const uintptr_t ra = reinterpret_cast<uintptr_t>(residual);
+    const uintptr_t oa = reinterpret_cast<uintptr_t>(other);
     const int chunks_max = static_cast<int>((hidden + 7) / 8 + 1);
-    const int stage_bytes = 2 * chunks_max * 16;
+    const int stage_bytes = (residual ? 2 : 1) * chunks_max * 16;
     const int row_phase = static_cast<int>((xa & 15u) >> 1);
     const StagedLayout fixed = staged_layout(0, stage_bytes, chunks_max);
     const int64_t room = static_cast<int64_t>(smem_limit) - fixed.total;
     int max_stages = room > 0 ? static_cast<int>(room / (stage_bytes + 2 * 8)) : 0;
     if (max_stages > kStagedMaxStages) max_stages = kStagedMaxStages;
 
-    if ((xa & 15u) == (ra & 15u) && max_stages >= 2) {
+    if ((xa & 15u) == (oa & 15u) && max_stages >= 2) {
         const int grid = static_cast<int>(rows < sm_count ? rows : sm_count);
         const int64_t rows_per_cta = (rows + grid - 1) / grid;
         // Ring depth S and consumer groups G (W = 16 / G warps per row), from a sweep of both on
@@ -175,12 +180,8 @@ RmsPlan plan_rms(const void* x, const void* residual, int64_t rows, int64_t hidd
 #ifdef IPL_TUNING_FORCE_STAGES
         if (stages > IPL_TUNING_FORCE_STAGES) stages = IPL_TUNING_FORCE_STAGES;
 #endif
-        const int warps_per_row = kStagedConsumerWarps / groups;
-        plan.kernel = warps_per_row == 1   ? RmsKernel::kStaged1
-                      : warps_per_row == 2 ? RmsKernel::kStaged2
-                      : warps_per_row == 4 ? RmsKernel::kStaged4
-                      : warps_per_row == 8 ? RmsKernel::kStaged8
-                                           : RmsKernel::kStaged16;
+        plan.family = RmsFamily::kStaged;
+        plan.warps_per_row = kStagedConsumerWarps / groups;
         plan.grid = static_cast<unsigned>(grid);
         plan.staged.rows = rows;
         plan.staged.hidden = static_cast<int>(hidden);
@@ -191,28 +192,79 @@ RmsPlan plan_rms(const void* x, const void* residual, int64_t rows, int64_t hidd
         plan.smem = staged_layout(stages, stage_bytes, chunks_max).total;
         return plan;
     }
-    plan.kernel = hidden <= static_cast<int64_t>(kRowwiseThreads) * kRowwiseCachedPerThread
-                      ? RmsKernel::kRowwiseCached
-                      : RmsKernel::kRowwiseTwoPass;
+    plan.family = hidden <= static_cast<int64_t>(kRowwiseThreads) * kRowwiseCachedPerThread
+                      ? RmsFamily::kRowwiseCached
+                      : RmsFamily::kRowwiseTwoPass;
     const int64_t cap = static_cast<int64_t>(sm_count) * 8;
     plan.grid = static_cast<unsigned>(rows < cap ? rows : cap);
     return plan;
 }
 
-template <int W>
-ipl_status launch_staged(const RmsPlan& plan, DeviceInfo* info, int bit, cudaStream_t stream) {
-    auto kernel = rmsnorm_staged_kernel<W>;
+template <int W, bool kResidual>
+ipl_status launch_staged(const RmsPlan& plan, DeviceInfo* info, cudaStream_t stream) {
+    auto kernel = rmsnorm_staged_kernel<W, kResidual>;
+    int bit = 0;
+    while ((1 << bit) < W) ++bit;
+    bit += kResidual ? 0 : 8;
     if (!(info->smem_configured.load(std::memory_order_acquire) & (1u << bit))) {
         const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                      info->max_smem_optin.load());
         if (err != cudaSuccess) {
-            return fail(IPL_ERROR_CUDA, "fused RMSNorm kernel setup failed: %s", cudaGetErrorString(err));
+            return fail(IPL_ERROR_CUDA, "%s kernel setup failed: %s", kResidual ? "fused RMSNorm" : "RMSNorm",
+                        cudaGetErrorString(err));
         }
         info->smem_configured.fetch_or(1u << bit, std::memory_order_acq_rel);
     }
     const cudaError_t err = launch(kernel, plan.grid, kStagedThreads, plan.smem, stream, plan.staged);
     if (err != cudaSuccess) {
-        return fail(IPL_ERROR_CUDA, "fused RMSNorm kernel launch failed: %s", cudaGetErrorString(err));
+        return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", kResidual ? "fused RMSNorm" : "RMSNorm",
+                    cudaGetErrorString(err));
+    }
+    return IPL_SUCCESS;
+}
+
+template <bool kResidual>
+ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, const uint16_t* weight, int64_t rows,
+                   int64_t hidden, double epsilon, cudaStream_t stream) {
+    int device = 0;
+    DeviceInfo* info = nullptr;
+    ipl_status st = current_device(&device, &info);
+    if (st != IPL_SUCCESS) return st;
+    RmsPlan plan = plan_rms(x, kResidual ? static_cast<const void*>(residual) : static_cast<const void*>(out), rows,
+                            hidden, kResidual, info->sm_count.load(std::memory_order_relaxed),
+                            info->max_smem_optin.load(std::memory_order_relaxed));
+    plan.staged.x = x;
+    plan.staged.residual = residual;
+    plan.staged.out = out;
+    plan.staged.weight = weight;
+    plan.staged.epsilon = static_cast<float>(epsilon);
+    switch (plan.family) {
+        case RmsFamily::kStaged:
+            switch (plan.warps_per_row) {
+                case 1: return launch_staged<1, kResidual>(plan, info, stream);
+                case 2: return launch_staged<2, kResidual>(plan, info, stream);
+                case 4: return launch_staged<4, kResidual>(plan, info, stream);
+                case 8: return launch_staged<8, kResidual>(plan, info, stream);
+                default: return launch_staged<16, kResidual>(plan, info, stream);
+            }
+        case RmsFamily::kRowwiseCached:
+        case RmsFamily::kRowwiseTwoPass: {
+            const cudaError_t err =
+                plan.family == RmsFamily::kRowwiseCached
+                    ? launch(rmsnorm_rowwise_kernel<true, kResidual>, plan.grid, kRowwiseThreads, 0, stream,
+                             static_cast<const uint16_t*>(x), residual, out, weight, rows, static_cast<int>(hidden),
+                             plan.staged.epsilon)
+                    : launch(rmsnorm_rowwise_kernel<false, kResidual>, plan.grid, kRowwiseThreads, 0, stream,
+                             static_cast<const uint16_t*>(x), residual, out, weight, rows, static_cast<int>(hidden),
+                             plan.staged.epsilon);
+            if (err != cudaSuccess) {
+                return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", kResidual ? "fused RMSNorm" : "RMSNorm",
+                            cudaGetErrorString(err));
+            }
+            return IPL_SUCCESS;
+        }
+        case RmsFamily::kNone:
+            return IPL_SUCCESS;
     }
     return IPL_SUCCESS;
 }
@@ -336,47 +388,21 @@ using namespace ipl;
 extern "C" {
 
 ipl_status ipl_fused_add_rms_norm_bf16(void* x, void* residual, const void* weight, int64_t rows,
-                                       int64_t hidden_size, double epsilon, void* stream_ptr) {
-    ipl_status st = check_rms_args(x, residual, weight, rows, hidden_size, epsilon);
-    if (st != IPL_SUCCESS) return st;
-    if (rows == 0) return IPL_SUCCESS;
-    int device = 0;
-    DeviceInfo* info = nullptr;
-    st = current_device(&device, &info);
-    if (st != IPL_SUCCESS) return st;
-    RmsPlan plan = plan_rms(x, residual, rows, hidden_size,
-                            info->sm_count.load(std::memory_order_relaxed),
-                            info->max_smem_optin.load(std::memory_order_relaxed));
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-    plan.staged.x = static_cast<uint16_t*>(x);
-    plan.staged.residual = static_cast<uint16_t*>(residual);
-    plan.staged.weight = static_cast<const uint16_t*>(weight);
-    plan.staged.epsilon = static_cast<float>(epsilon);
-    switch (plan.kernel) {
-        case RmsKernel::kStaged1: return launch_staged<1>(plan, info, 0, stream);
-        case RmsKernel::kStaged2: return launch_staged<2>(plan, info, 1, stream);
-        case RmsKernel::kStaged4: return launch_staged<4>(plan, info, 2, stream);
-        case RmsKernel::kStaged8: return launch_staged<8>(plan, info, 3, stream);
-        case RmsKernel::kStaged16: return launch_staged<16>(plan, info, 4, stream);
-        case RmsKernel::kRowwiseCached:
-        case RmsKernel::kRowwiseTwoPass: {
-            const cudaError_t err =
-                plan.kernel == RmsKernel::kRowwiseCached
-                    ? launch(rmsnorm_rowwise_kernel<true>, plan.grid, kRowwiseThreads, 0, stream,
-                             plan.staged.x, plan.staged.residual, plan.staged.weight, rows,
-                             static_cast<int>(hidden_size), plan.staged.epsilon)
-                    : launch(rmsnorm_rowwise_kernel<false>, plan.grid, kRowwiseThreads, 0, stream,
-                             plan.staged.x, plan.staged.residual, plan.staged.weight, rows,
-                             static_cast<int>(hidden_size), plan.staged.epsilon);
-            if (err != cudaSuccess) {
-                return fail(IPL_ERROR_CUDA, "fused RMSNorm kernel launch failed: %s", cudaGetErrorString(err));
-            }
-            return IPL_SUCCESS;
-        }
-        case RmsKernel::kNone:
-            return IPL_SUCCESS;
-    }
-    return IPL_SUCCESS;
+                                       int64_t hidden_size, double epsilon, void* stream) {
+    const ipl_status st = check_rms_args(x, residual, weight, rows, hidden_size, epsilon, true);
+    if (st != IPL_SUCCESS || rows == 0) return st;
+    return run_rms<true>(static_cast<uint16_t*>(x), static_cast<uint16_t*>(residual), static_cast<uint16_t*>(x),
+                         static_cast<const uint16_t*>(weight), rows, hidden_size, epsilon,
+                         static_cast<cudaStream_t>(stream));
+}
+
+ipl_status ipl_rms_norm_bf16(void* output, const void* input, const void* weight, int64_t rows,
+                             int64_t hidden_size, double epsilon, void* stream) {
+    const ipl_status st = check_rms_args(input, output, weight, rows, hidden_size, epsilon, false);
+    if (st != IPL_SUCCESS || rows == 0) return st;
+    return run_rms<false>(const_cast<uint16_t*>(static_cast<const uint16_t*>(input)), nullptr,
+                          static_cast<uint16_t*>(output), static_cast<const uint16_t*>(weight), rows, hidden_size,
+                          epsilon, static_cast<cudaStream_t>(stream));
 }
 
 ipl_status ipl_silu_and_mul_bf16(void* output, const void* input, int64_t rows, int64_t intermediate_size,
@@ -435,9 +461,15 @@ ipl_status ipl_clear_device_fault_flags(int device) {
 
 const char* ipl_fused_add_rms_norm_plan(const void* x, const void* residual, const void* weight, int64_t rows,
                                         int64_t hidden_size) {
-    if (check_rms_args(x, residual, weight, rows, hidden_size, 1.0) != IPL_SUCCESS) return "invalid";
+    if (check_rms_args(x, residual, weight, rows, hidden_size, 1.0, true) != IPL_SUCCESS) return "invalid";
     // B200 limits: 148 SMs, 232448 bytes of opt-in shared memory per block.
-    return rms_kernel_name(plan_rms(x, residual, rows, hidden_size, 148, 232448).kernel);
+    return rms_kernel_name(plan_rms(x, residual, rows, hidden_size, true, 148, 232448), true);
+}
+
+const char* ipl_rms_norm_plan(const void* output, const void* input, const void* weight, int64_t rows,
+                              int64_t hidden_size) {
+    if (check_rms_args(input, output, weight, rows, hidden_size, 1.0, false) != IPL_SUCCESS) return "invalid";
+    return rms_kernel_name(plan_rms(input, output, rows, hidden_size, false, 148, 232448), false);
 }
 
 const char* ipl_silu_and_mul_plan(const void* output, const void* input, int64_t rows,

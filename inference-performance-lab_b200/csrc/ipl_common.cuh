@@ -136,6 +136,12 @@ __device__ __forceinline__ U32x4 lds_v4(uint32_t addr) {
                  : "r"(addr));
     return r;
 }
+__device__ __forceinline__ void sts_pairs(uint32_t addr, F32x2 a, F32x2 b) {
+    asm volatile("st.shared.v2.b64 [%0], {%1, %2};" ::"r"(addr), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void lds_pairs(uint32_t addr, F32x2& a, F32x2& b) {
+    asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr) : "memory");
+}
 __device__ __forceinline__ float lds_f32(uint32_t addr) {
     float r;
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"(addr));
@@ -162,14 +168,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                  : "memory");
 }
+// Tests the phase; if it is not complete the thread is suspended (it issues nothing) until the
+// phase completes or about kWaitSliceNs pass, so waiting warps leave the issue slots to working
+// ones.
+constexpr uint32_t kWaitSliceNs = 100000;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(kWaitSliceNs)
         : "memory");
     return done != 0;
 }
@@ -181,15 +191,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
                                                   volatile int* abort, uint32_t fault_bit) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = global_timer_ns();
-    for (uint32_t spin = 1;; ++spin) {
+    for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((spin & 63u) == 0) {
-            if (*abort) return false;
-            if (global_timer_ns() - start > kWaitLimitNs) {
-                atomicOr(&g_fault_word, fault_bit);
-                *abort = 1;
-                return false;
-            }
+        if (*abort) return false;
+        if (global_timer_ns() - start > kWaitLimitNs) {
+            atomicOr(&g_fault_word, fault_bit);
+            *abort = 1;
+            return false;
         }
     }
 }

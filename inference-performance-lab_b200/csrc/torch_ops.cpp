@@ -109,6 +109,34 @@ void fused_add_rms_norm_cuda(ts::Tensor& x, ts::Tensor& residual, const ts::Tens
                                                weight.const_data_ptr(), rows, hidden_size, epsilon, stream));
 }
 
+void rms_norm_cuda(ts::Tensor& output, const ts::Tensor& input, const ts::Tensor& weight, double epsilon) {
+    STD_TORCH_CHECK(output.is_cuda() && input.is_cuda() && weight.is_cuda(),
+                    "output, input, and weight must be CUDA tensors");
+    STD_TORCH_CHECK(output.scalar_type() == torch::headeronly::ScalarType::BFloat16 &&
+                        input.scalar_type() == torch::headeronly::ScalarType::BFloat16 &&
+                        weight.scalar_type() == torch::headeronly::ScalarType::BFloat16,
+                    "output, input, and weight must use bfloat16");
+    STD_TORCH_CHECK(output.is_contiguous() && input.is_contiguous() && weight.is_contiguous(),
+                    "output, input, and weight must be contiguous");
+    STD_TORCH_CHECK(output.sizes().equals(input.sizes()), "output and input must have identical shapes");
+    STD_TORCH_CHECK(output.device() == input.device() && input.device() == weight.device(),
+                    "output, input, and weight must be on the same device");
+    STD_TORCH_CHECK(input.dim() >= 1, "input must have at least one dimension");
+    STD_TORCH_CHECK(weight.dim() == 1, "weight must be one-dimensional");
+    STD_TORCH_CHECK(weight.size(0) == input.size(-1), "weight must match the final tensor dimension");
+    STD_TORCH_CHECK(epsilon > 0.0, "epsilon must be positive");
+    if (input.numel() == 0) {
+        return;
+    }
+    const int64_t hidden_size = input.size(-1);
+    const int64_t rows = input.numel() / hidden_size;
+    const int32_t device = input.get_device_index();
+    const ts::accelerator::DeviceGuard device_guard(device);
+    void* stream = current_stream(device);
+    raise_on_error(ipl_rms_norm_bf16(output.mutable_data_ptr(), input.const_data_ptr(), weight.const_data_ptr(),
+                                     rows, hidden_size, epsilon, stream));
+}
+
 void silu_and_mul_cuda(ts::Tensor& output, const ts::Tensor& input) { run_silu(output, input, false); }
 
 void silu_and_mul_packed_cuda(ts::Tensor& output, const ts::Tensor& input) { run_silu(output, input, true); }
@@ -117,10 +145,13 @@ STABLE_TORCH_LIBRARY(inference_performance_lab, library) {
     library.def("fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor weight, float epsilon) -> ()");
     library.def("silu_and_mul(Tensor(a!) output, Tensor input) -> ()");
     library.def("silu_and_mul_packed(Tensor(a!) output, Tensor input) -> ()");
+    // Not in the reference library: plain RMSNorm (vLLM's _C.rms_norm argument order).
+    library.def("rms_norm(Tensor(a!) output, Tensor input, Tensor weight, float epsilon) -> ()");
 }
 
 STABLE_TORCH_LIBRARY_IMPL(inference_performance_lab, CUDA, library) {
     library.impl("fused_add_rms_norm", TORCH_BOX(&fused_add_rms_norm_cuda));
     library.impl("silu_and_mul", TORCH_BOX(&silu_and_mul_cuda));
     library.impl("silu_and_mul_packed", TORCH_BOX(&silu_and_mul_packed_cuda));
+    library.impl("rms_norm", TORCH_BOX(&rms_norm_cuda));
 }

@@ -32,6 +32,18 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             ctypes.c_void_p,
         ],
     ),
+    "ipl_rms_norm_bf16": (
+        ctypes.c_int,
+        [
+            ctypes.c_void_p,
+            ctypes.c_void_p,
+            ctypes.c_void_p,
+            ctypes.c_int64,
+            ctypes.c_int64,
+            ctypes.c_double,
+            ctypes.c_void_p,
+        ],
+    ),
     "ipl_silu_and_mul_bf16": (
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p],
@@ -46,6 +58,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ipl_device_fault_flags": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]),
     "ipl_clear_device_fault_flags": (ctypes.c_int, [ctypes.c_int]),
     "ipl_fused_add_rms_norm_plan": (
+        ctypes.c_char_p,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64],
+    ),
+    "ipl_rms_norm_plan": (
         ctypes.c_char_p,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64],
     ),
@@ -97,6 +113,20 @@ def fused_add_rms_norm(
     )
 
 
+def rms_norm(
+    output_ptr: int,
+    input_ptr: int,
+    weight_ptr: int,
+    rows: int,
+    hidden_size: int,
+    epsilon: float,
+    stream: int = 0,
+) -> None:
+    _check(
+        library().ipl_rms_norm_bf16(output_ptr, input_ptr, weight_ptr, rows, hidden_size, epsilon, stream)
+    )
+
+
 def silu_and_mul(
     output_ptr: int, input_ptr: int, rows: int, intermediate_size: int, stream: int = 0
 ) -> None:
@@ -131,6 +161,10 @@ def fused_add_rms_norm_plan(
     ).decode()
 
 
+def rms_norm_plan(output_ptr: int, input_ptr: int, weight_ptr: int, rows: int, hidden_size: int) -> str:
+    return library().ipl_rms_norm_plan(output_ptr, input_ptr, weight_ptr, rows, hidden_size).decode()
+
+
 def silu_and_mul_plan(output_ptr: int, input_ptr: int, rows: int, intermediate_size: int) -> str:
     return library().ipl_silu_and_mul_plan(output_ptr, input_ptr, rows, intermediate_size).decode()
 
@@ -149,6 +183,14 @@ def fused_add_rms_norm_tensors(x, residual, weight, epsilon: float) -> None:
     rows = x.numel() // hidden if hidden else 0
     fused_add_rms_norm(
         x.data_ptr(), residual.data_ptr(), weight.data_ptr(), rows, hidden, epsilon, _stream_handle()
+    )
+
+
+def rms_norm_tensors(output, input_, weight, epsilon: float) -> None:
+    hidden = input_.shape[-1]
+    rows = input_.numel() // hidden if hidden else 0
+    rms_norm(
+        output.data_ptr(), input_.data_ptr(), weight.data_ptr(), rows, hidden, epsilon, _stream_handle()
     )
 
 

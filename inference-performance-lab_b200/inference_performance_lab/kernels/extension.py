@@ -65,6 +65,16 @@ def fused_add_rms_norm(
     torch.ops.inference_performance_lab.fused_add_rms_norm(x, residual, weight, epsilon)
 
 
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, epsilon: float) -> torch.Tensor:
+    """``rmsnorm(x) * weight`` into a new tensor (no residual; not in the reference library)."""
+    load_extension()
+
+    output = torch.empty_like(x)
+    torch.ops.inference_performance_lab.rms_norm(output, x, weight, epsilon)
+
+    return output
+
+
 def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
     """``silu(x[..., :I]) * x[..., I:]`` into a new ``[..., I]`` tensor (any width/alignment)."""
     load_extension()

@@ -1,4 +1,5 @@
-"""vLLM general plugin: the ``inference_lab`` provider of ``vllm.ir.ops.fused_add_rms_norm``.
+"""vLLM general plugin: the ``inference_lab`` provider of ``vllm.ir.ops.fused_add_rms_norm`` and
+``vllm.ir.ops.rms_norm``.
 
 Same entry point, provider name and registration as the reference
 (src/inference_performance_lab/kernels/vllm_plugin.py:11,43-69; entry point
@@ -6,7 +7,8 @@ Same entry point, provider name and registration as the reference
 The argument filter is wider: the reference accepted only 2-D inputs with hidden size 3584
 (:15-40, the one shape its specialised kernel handled); the B200 kernels take any hidden size and
 alignment, so any contiguous bf16 input on one CUDA device with a weight and no
-``variance_size`` is accepted.
+``variance_size`` is accepted. The plain ``rms_norm`` provider (not in the reference; the norm
+before the first and after the last decoder layer) follows the same rules.
 """
 
 from __future__ import annotations
@@ -18,6 +20,7 @@ from inference_performance_lab.kernels.extension import (
     fused_add_rms_norm as custom_fused_add_rms_norm,
 )
 from inference_performance_lab.kernels.extension import load_extension
+from inference_performance_lab.kernels.extension import rms_norm as custom_rms_norm
 
 PROVIDER = "inference_lab"
 
@@ -51,14 +54,35 @@ def supports_fused_add_rms_norm(
     )
 
 
+def supports_rms_norm(
+    x: Tensor, weight: Tensor | None, epsilon: float, variance_size: int | None = None
+) -> bool:
+    del epsilon
+
+    return (
+        variance_size is None
+        and weight is not None
+        and x.device.type == "cuda"
+        and weight.device == x.device
+        and x.dtype == torch.bfloat16
+        and weight.dtype == x.dtype
+        and x.ndim >= 1
+        and x.shape[-1] > 0
+        and weight.shape == (x.shape[-1],)
+        and x.is_contiguous()
+        and weight.is_contiguous()
+    )
+
+
 def register() -> None:
     from vllm import ir
+
+    load_extension()
+    _register_rms_norm(ir.ops.rms_norm)
 
     op = ir.ops.fused_add_rms_norm
     if PROVIDER in op.impls:
         return
-
-    load_extension()
 
     @op.register_impl(
         PROVIDER,
@@ -78,3 +102,17 @@ def register() -> None:
 
         custom_fused_add_rms_norm(x, x_residual, weight, epsilon)
         return x, x_residual
+
+
+def _register_rms_norm(op) -> None:
+    if PROVIDER in op.impls:
+        return
+
+    @op.register_impl(PROVIDER, supported=torch.cuda.is_available(), supports_args=supports_rms_norm)
+    def inference_lab_rms_norm(
+        x: Tensor, weight: Tensor | None, epsilon: float, variance_size: int | None = None
+    ) -> Tensor:
+        assert weight is not None
+        assert variance_size is None
+
+        return custom_rms_norm(x, weight, epsilon)

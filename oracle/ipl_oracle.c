@@ -11,6 +11,9 @@
  *     output = residual_out_fp32 * inverse_rms * weight.float()              (:21)
  *     return output.to(bf16), residual_out_fp32.to(bf16)                     (:23)
  *
+ *   plain RMSNorm (no counterpart in the reference; its arithmetic with no residual term):
+ *     v = x.float(); output = v * rsqrt(v.square().mean(-1) + epsilon) * weight.float()
+ *
  *   silu_and_mul_reference (reference.py:26-35):
  *     gate, up = x.float().chunk(2, -1); output = silu(gate) * up; output.to(bf16)  (:32-35)
  *
@@ -71,6 +74,29 @@ int oracle_fused_add_rms_norm_bf16(const uint16_t* x, const uint16_t* residual, 
         }
     }
     free(v);
+    return 0;
+}
+
+/* Plain RMSNorm: reference.py:19-23 applied to x itself (no residual add, no residual output). */
+int oracle_rms_norm_bf16(const uint16_t* x, const uint16_t* weight, int64_t rows, int64_t hidden, double epsilon,
+                         uint16_t* out) {
+    if (rows <= 0 || hidden <= 0) return 0;
+    const float eps = (float)epsilon;
+    for (int64_t r = 0; r < rows; ++r) {
+        const uint16_t* xr = x + r * hidden;
+        double acc = 0.0;
+        for (int64_t c = 0; c < hidden; ++c) {
+            const float value = bf16_to_f32(xr[c]);
+            const float square = value * value;
+            acc += (double)square;
+        }
+        const float mean = (float)(acc / (double)hidden);
+        const float inverse_rms = 1.0f / sqrtf(mean + eps);
+        for (int64_t c = 0; c < hidden; ++c) {
+            const float scaled = bf16_to_f32(xr[c]) * inverse_rms;
+            out[r * hidden + c] = f32_to_bf16(scaled * bf16_to_f32(weight[c]));
+        }
+    }
     return 0;
 }
 

@@ -45,6 +45,8 @@ def _lib() -> ctypes.CDLL:
     lib.oracle_fused_add_rms_norm_bf16.argtypes = [
         _U16P, _U16P, _U16P, ctypes.c_int64, ctypes.c_int64, ctypes.c_double, _U16P, _U16P,
     ]
+    lib.oracle_rms_norm_bf16.restype = ctypes.c_int
+    lib.oracle_rms_norm_bf16.argtypes = [_U16P, _U16P, ctypes.c_int64, ctypes.c_int64, ctypes.c_double, _U16P]
     lib.oracle_silu_and_mul_bf16.restype = None
     lib.oracle_silu_and_mul_bf16.argtypes = [_U16P, ctypes.c_int64, ctypes.c_int64, _U16P]
     lib.oracle_f32_to_bf16.restype = ctypes.c_uint16
@@ -83,6 +85,19 @@ def c_fused_add_rms_norm(
         if status != 0:
             raise MemoryError("oracle scratch allocation failed")
     return out, res
+
+
+def c_rms_norm(x: np.ndarray, weight: np.ndarray, epsilon: float) -> np.ndarray:
+    """Plain RMSNorm (no residual) as uint16 bf16 bit patterns."""
+    x, weight = _u16(x), _u16(weight)
+    if weight.ndim != 1 or x.ndim == 0 or weight.shape[0] != x.shape[-1]:
+        raise ValueError("weight must match the final tensor dimension")
+    hidden = x.shape[-1]
+    rows = x.size // hidden if hidden else 0
+    out = np.empty_like(x)
+    if rows and hidden:
+        _lib().oracle_rms_norm_bf16(_ptr(x), _ptr(weight), rows, hidden, epsilon, _ptr(out))
+    return out
 
 
 def c_silu_and_mul(x: np.ndarray) -> np.ndarray:
@@ -125,6 +140,17 @@ def torch_fused_add_rms_norm(x, residual, weight, epsilon: float):
     summed = x.float() + residual.float()
     inverse_rms = torch.rsqrt(summed.square().mean(dim=-1, keepdim=True) + epsilon)
     return (summed * inverse_rms * weight.float()).to(x.dtype), summed.to(residual.dtype)
+
+
+def torch_rms_norm(x, weight, epsilon: float):
+    """Plain RMSNorm in the reference oracle's fp32 arithmetic (reference.py:19-23, no residual)."""
+    import torch
+
+    if weight.ndim != 1 or weight.shape[0] != x.shape[-1]:
+        raise ValueError("weight must match the final tensor dimension")
+    v = x.float()
+    inverse_rms = torch.rsqrt(v.square().mean(dim=-1, keepdim=True) + epsilon)
+    return (v * inverse_rms * weight.float()).to(x.dtype)
 
 
 def torch_silu_and_mul(x):

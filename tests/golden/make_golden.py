@@ -84,6 +84,22 @@ def main() -> None:
         arrays[f"{name}.residual_out"] = bits(res)
         meta[name] = {"op": "fused_add_rms_norm", "rows": rows, "hidden": hidden, "epsilon": eps}
 
+    # Plain RMSNorm: the reference oracle's arithmetic with a zero residual (x + 0 is x for every
+    # nonzero x; the inputs hold no zeros, so the sign of zero never matters).
+    plain_cases = [
+        ("rms_plain_3584", 8, 3584, 1e-6, 10),
+        ("rms_plain_odd_width", 5, 1001, 1e-6, 11),
+        ("rms_plain_8192", 2, 8192, 1e-5, 12),
+    ]
+    for name, rows, hidden, eps, seed in plain_cases:
+        x, _, weight = rms_inputs(rows, hidden, seed)
+        assert bool((x != 0).all())
+        out, _ = ref.fused_add_rms_norm_reference(x, torch.zeros_like(x), weight, eps)
+        arrays[f"{name}.x"] = bits(x)
+        arrays[f"{name}.weight"] = bits(weight)
+        arrays[f"{name}.out"] = bits(out)
+        meta[name] = {"op": "rms_norm", "rows": rows, "hidden": hidden, "epsilon": eps}
+
     silu_cases = [
         # name, rows, intermediate, seed, std
         ("silu_width18944", 2, 18944, 0, 2.0),

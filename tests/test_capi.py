@@ -67,6 +67,27 @@ def test_rms_argument_errors(args, status, message) -> None:
     assert info.value.status == status
 
 
+@pytest.mark.parametrize(
+    "args, message",
+    [
+        ((BASE, BASE + 4096, BASE + 8192, 4, 3584, 0.0), "epsilon must be positive"),
+        ((0, BASE + 4096, BASE + 8192, 4, 3584, 1e-6), "output, input and weight must be non-null"),
+        ((BASE, BASE + 4096, BASE + 8192, 4, 0, 1e-6), "non-empty final dimension"),
+        ((BASE + 1, BASE + 4096, BASE + 8192, 4, 16, 1e-6), "2-byte aligned"),
+    ],
+)
+def test_plain_rms_argument_errors(args, message) -> None:
+    with pytest.raises(capi.IplError, match=message):
+        capi.rms_norm(*args)
+
+
+def test_plain_rms_in_place_is_accepted_by_the_plan() -> None:
+    # output == input is allowed (vLLM calls it out of place, callers may reuse the buffer).
+    assert capi.rms_norm_plan(BASE, BASE, BASE + 8192, 2048, 3584) == "rmsnorm_staged_kernel<2, plain>"
+    assert capi.rms_norm_plan(BASE + 2, BASE, BASE + 8192, 8, 3584) == "rmsnorm_rowwise_kernel<cached, plain>"
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 1, 8192) == "rmsnorm_staged_kernel<16, plain>"
+
+
 def test_rms_empty_batch_is_a_no_op() -> None:
     # rows == 0 returns before any device query.
     capi.fused_add_rms_norm(0, 0, 0, 0, 3584, 1e-6)

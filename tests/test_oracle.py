@@ -21,6 +21,7 @@ GOLDEN = np.load(GOLDEN_DIR / "golden.npz")
 CASES = json.loads((GOLDEN_DIR / "golden.json").read_text())["cases"]
 RMS_CASES = sorted(name for name, meta in CASES.items() if meta["op"] == "fused_add_rms_norm")
 SILU_CASES = sorted(name for name, meta in CASES.items() if meta["op"] == "silu_and_mul")
+PLAIN_CASES = sorted(name for name, meta in CASES.items() if meta["op"] == "rms_norm")
 
 
 def test_golden_covers_the_reference_cpu_configuration() -> None:
@@ -37,6 +38,14 @@ def test_c_oracle_matches_reference_rms(name: str) -> None:
     )
     np.testing.assert_array_equal(res, GOLDEN[f"{name}.residual_out"])
     np.testing.assert_array_equal(out, GOLDEN[f"{name}.out"])
+
+
+@pytest.mark.parametrize("name", PLAIN_CASES)
+def test_oracles_match_reference_plain_rms_norm(name: str) -> None:
+    x, w, eps = GOLDEN[f"{name}.x"], GOLDEN[f"{name}.weight"], CASES[name]["epsilon"]
+    np.testing.assert_array_equal(oracle.c_rms_norm(x, w, eps), GOLDEN[f"{name}.out"])
+    out = oracle.torch_rms_norm(oracle.bits_tensor(x), oracle.bits_tensor(w), eps)
+    np.testing.assert_array_equal(oracle.tensor_bits(out), GOLDEN[f"{name}.out"])
 
 
 @pytest.mark.parametrize("name", SILU_CASES)

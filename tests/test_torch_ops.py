@@ -81,3 +81,15 @@ def test_shim_shares_torchs_libstdcxx() -> None:
         ["readelf", "-d", str(extension.TORCH_OPS_LIBRARY)], capture_output=True, text=True, check=True
     ).stdout
     assert "libstdc++.so.6" in needed
+
+
+def test_vllm_rms_norm_provider_registers() -> None:
+    pytest.importorskip("vllm.ir")
+    from vllm import ir
+
+    from inference_performance_lab.kernels import vllm_plugin
+
+    vllm_plugin.register()
+    assert vllm_plugin.PROVIDER in ir.ops.rms_norm.impls
+    x = torch.zeros(4, 3584, dtype=torch.bfloat16)
+    assert not vllm_plugin.supports_rms_norm(x, torch.ones(3584, dtype=torch.bfloat16), 1e-6)
