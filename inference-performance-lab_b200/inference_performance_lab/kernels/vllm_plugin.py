@@ -116,3 +116,40 @@ def _register_rms_norm(op) -> None:
         assert variance_size is None
 
         return custom_rms_norm(x, weight, epsilon)
+
+
+def supports_silu_and_mul(x: Tensor) -> bool:
+    return (
+        x.device.type == "cuda"
+        and x.dtype == torch.bfloat16
+        and x.ndim >= 1
+        and x.shape[-1] % 2 == 0
+        and x.is_contiguous()
+    )
+
+
+def register_silu_and_mul() -> None:
+    """Replace vLLM's SiluAndMul custom op with one that runs these kernels.
+
+    vLLM 0.22 has no IR op for SiLU-and-mul, so the replacement goes through its out-of-tree
+    custom-op registry: every ``SiluAndMul`` a model builds afterwards is this subclass, whose
+    CUDA path calls ``torch.ops.inference_performance_lab.silu_and_mul`` for contiguous bf16
+    inputs and vLLM's own kernel otherwise. It is a separate entry point (not called by
+    :func:`register`) because, unlike the IR providers, it takes effect without a priority list.
+    """
+    from vllm.model_executor.custom_op import op_registry_oot
+    from vllm.model_executor.layers.activation import SiluAndMul
+
+    if "SiluAndMul" in op_registry_oot:
+        return
+
+    load_extension()
+
+    @SiluAndMul.register_oot(name="SiluAndMul")
+    class InferenceLabSiluAndMul(SiluAndMul):
+        def forward_cuda(self, x: Tensor) -> Tensor:
+            if not supports_silu_and_mul(x):
+                return super().forward_cuda(x)
+            output = torch.empty(x.shape[:-1] + (x.shape[-1] // 2,), dtype=x.dtype, device=x.device)
+            torch.ops.inference_performance_lab.silu_and_mul(output, x)
+            return output

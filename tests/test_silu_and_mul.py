@@ -183,3 +183,30 @@ def test_graph_capture() -> None:
     torch.cuda.synchronize()
     assert_close_to_oracle(out, oracle.c_silu_and_mul(oracle.tensor_bits(x)), "graph")
     del graph
+
+
+@pytest.mark.vllm
+@torch.inference_mode()
+def test_vllm_silu_and_mul_layer_runs_the_b200_kernel() -> None:
+    """vLLM's SiluAndMul layer, replaced through its out-of-tree custom-op registry, returns these
+    kernels' result (bit-identical to the op) and matches the oracle and vLLM's native path."""
+    pytest.importorskip("vllm.model_executor.layers.activation")
+    from vllm.config import VllmConfig, set_current_vllm_config
+    from vllm.model_executor.layers.activation import SiluAndMul
+
+    from inference_performance_lab.kernels import vllm_plugin
+
+    vllm_plugin.register_silu_and_mul()
+    vllm_plugin.register_silu_and_mul()  # idempotent
+    with set_current_vllm_config(VllmConfig()):
+        layer = SiluAndMul()
+    assert type(layer).__name__ == "InferenceLabSiluAndMul"
+    torch.manual_seed(4)
+    x = (torch.randn(128, 37888, device="cuda") * 2).to(torch.bfloat16)
+    y = layer.forward_cuda(x)
+    assert torch.equal(y, custom_silu_and_mul(x))
+    assert_close_to_oracle(y, oracle.c_silu_and_mul(oracle.tensor_bits(x)), "vLLM SiluAndMul")
+    torch.testing.assert_close(y, SiluAndMul.forward_native(x), rtol=1e-2, atol=1e-2)
+    # Inputs the kernels do not take go to vLLM's own kernel.
+    x16 = x.to(torch.float16)
+    torch.testing.assert_close(layer.forward_cuda(x16), SiluAndMul.forward_native(x16), rtol=1e-2, atol=1e-2)
