@@ -81,11 +81,12 @@ cudaError_t launch(Kernel kernel, unsigned grid, unsigned block, size_t smem, cu
 // ------------------------------------------------------------------------------------------
 // add + RMSNorm / RMSNorm planning
 
-enum class RmsFamily { kNone, kStaged, kRowwiseCached, kRowwiseTwoPass };
+enum class RmsFamily { kNone, kStaged, kWarpRow, kRowwiseCached, kRowwiseTwoPass };
 
 struct RmsPlan {
     RmsFamily family = RmsFamily::kNone;
     int warps_per_row = 0;  // staged kernels: 1, 2, 4, 8 or 16
+    int chunks_per_lane = 0;  // warp-per-row kernel: 1, 2, 4 or 8
     unsigned grid = 0;
     size_t smem = 0;
     StagedParams staged = {};
@@ -104,6 +105,14 @@ const char* rms_kernel_name(const RmsPlan& plan, bool residual) {
             int i = 0;
             while ((1 << i) < plan.warps_per_row) ++i;
             return kStagedNames[residual ? 1 : 0][i];
+        }
+        case RmsFamily::kWarpRow: {
+            static const char* const kWarpNames[2][3] = {
+                {"rmsnorm_warp_kernel<1, plain>", "rmsnorm_warp_kernel<2, plain>", "rmsnorm_warp_kernel<4, plain>"},
+                {"rmsnorm_warp_kernel<1>", "rmsnorm_warp_kernel<2>", "rmsnorm_warp_kernel<4>"}};
+            int i = 0;
+            while ((1 << i) < plan.chunks_per_lane) ++i;
+            return kWarpNames[residual ? 1 : 0][i];
         }
         case RmsFamily::kRowwiseCached:
             return residual ? "rmsnorm_rowwise_kernel<cached>" : "rmsnorm_rowwise_kernel<cached, plain>";
@@ -150,6 +159,18 @@ RmsPlan plan_rms(const void* x, const void* other, int64_t rows, int64_t hidden,
     int max_stages = room > 0 ? static_cast<int>(room / (stage_bytes + 2 * 8)) : 0;
     if (max_stages > kStagedMaxStages) max_stages = kStagedMaxStages;
 
+    // Short aligned rows: a warp per row, values in registers.
+    if (hidden % 8 == 0 && hidden <= kWarpRowMaxHidden && ((xa | oa) & 15u) == 0) {
+        const int64_t per_lane = (hidden / 8 + kWarpSize - 1) / kWarpSize;
+        plan.family = RmsFamily::kWarpRow;
+        plan.chunks_per_lane = per_lane <= 1 ? 1 : per_lane <= 2 ? 2 : 4;
+        const int64_t warps_per_cta = kWarpRowThreads / kWarpSize;
+        const int64_t need = (rows + warps_per_cta - 1) / warps_per_cta;
+        const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+        plan.grid = static_cast<unsigned>(need < cap ? need : cap);
+        plan.smem = static_cast<size_t>(hidden) * 4u;
+        return plan;
+    }
     if ((xa & 15u) == (oa & 15u) && max_stages >= 2) {
         const int grid = static_cast<int>(rows < sm_count ? rows : sm_count);
         const int64_t rows_per_cta = (rows + grid - 1) / grid;
@@ -247,6 +268,27 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, const uint16_
                 case 8: return launch_staged<8, kResidual>(plan, info, stream);
                 default: return launch_staged<16, kResidual>(plan, info, stream);
             }
+        case RmsFamily::kWarpRow: {
+            WarpRowParams w;
+            w.x = x;
+            w.residual = residual;
+            w.out = out;
+            w.weight = weight;
+            w.rows = rows;
+            w.hidden = static_cast<int>(hidden);
+            w.epsilon = plan.staged.epsilon;
+            cudaError_t err = cudaSuccess;
+            switch (plan.chunks_per_lane) {
+                case 1: err = launch(rmsnorm_warp_kernel<1, kResidual>, plan.grid, kWarpRowThreads, plan.smem, stream, w); break;
+                case 2: err = launch(rmsnorm_warp_kernel<2, kResidual>, plan.grid, kWarpRowThreads, plan.smem, stream, w); break;
+                default: err = launch(rmsnorm_warp_kernel<4, kResidual>, plan.grid, kWarpRowThreads, plan.smem, stream, w); break;
+            }
+            if (err != cudaSuccess) {
+                return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", kResidual ? "fused RMSNorm" : "RMSNorm",
+                            cudaGetErrorString(err));
+            }
+            return IPL_SUCCESS;
+        }
         case RmsFamily::kRowwiseCached:
         case RmsFamily::kRowwiseTwoPass: {
             const cudaError_t err =

@@ -112,6 +112,14 @@ __device__ __forceinline__ U32x8 ld_stream_v8(const void* p) {
                  : "l"(p));
     return r;
 }
+// Coherent 16-byte load that does not allocate in L1 (the data may be rewritten by this kernel).
+__device__ __forceinline__ U32x4 ld_v4(const void* p) {
+    U32x4 r;
+    asm volatile("ld.global.L1::no_allocate.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3])
+                 : "l"(p));
+    return r;
+}
 __device__ __forceinline__ void st_v4(void* p, const U32x4& r) {
     asm volatile("st.global.v4.b32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(r.v[0]), "r"(r.v[1]),
                  "r"(r.v[2]), "r"(r.v[3])

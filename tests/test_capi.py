@@ -143,12 +143,18 @@ def test_rms_plan_selection() -> None:
     assert rms_plan(0, 0, 0, 148 * 4, 3584) == "rmsnorm_staged_kernel<4>"
     # Streaming (more rows than fit): about 128 KB in flight, one stage per group.
     assert rms_plan(0, 0, 0, 148 * 16, 3584) == "rmsnorm_staged_kernel<2>"
-    assert rms_plan(0, 0, 0, 148 * 64, 1024) == "rmsnorm_staged_kernel<1>"
+    # Short aligned rows: a warp per row.
+    assert rms_plan(0, 0, 0, 148 * 64, 1024) == "rmsnorm_warp_kernel<4>"
+    assert rms_plan(0, 0, 3, 5, 1000) == "rmsnorm_warp_kernel<4>"
+    assert rms_plan(0, 0, 0, 5, 2048).startswith("rmsnorm_staged_kernel")
+    assert rms_plan(0, 0, 0, 5, 256) == "rmsnorm_warp_kernel<1>"
+    assert rms_plan(1, 1, 0, 5, 1024).startswith("rmsnorm_staged_kernel")
     # The row-sharded workload's hidden size: four 32 KB rows in flight, 4 warps each.
     assert rms_plan(0, 0, 0, 262144, 8192) == "rmsnorm_staged_kernel<4>"
     assert rms_plan(0, 0, 0, 32768, 8192) == "rmsnorm_staged_kernel<4>"
     # Odd widths stay on the staged kernel when x and residual share their offset.
     assert rms_plan(0, 0, 0, 64, 1001).startswith("rmsnorm_staged_kernel")
+    assert rms_plan(0, 0, 0, 64, 2056).startswith("rmsnorm_staged_kernel")
     # Rows too long for two stages fall back to the two-pass row kernel.
     assert rms_plan(0, 0, 0, 64, 40000) == "rmsnorm_rowwise_kernel<two-pass>"
     assert rms_plan(1, 0, 0, 64, 40000) == "rmsnorm_rowwise_kernel<two-pass>"
