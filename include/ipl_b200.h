@@ -76,6 +76,26 @@ IPL_API ipl_status ipl_rms_norm_bf16(void* output, const void* input, const void
                                      int64_t hidden_size, double epsilon, void* stream);
 
 /*
+ * Fused residual add + RMSNorm with a statically scaled fp8 (e4m3) output:
+ *
+ *   v        = fp32(input) + fp32(residual)
+ *   residual = bf16(v)                                            (bit-exact, in place)
+ *   output   = e4m3(((v * rsqrt(mean(v^2) + epsilon)) * fp32(weight)) / *scale)
+ *
+ * e4m3 is OCP E4M3FN (bias 7, max 448, no infinities), round to nearest even, saturating to
+ * +-448. input is read only. output: [rows, hidden_size] bytes; scale: one fp32 on the device.
+ *
+ * No counterpart in the reference's C++ sources: it is the fused variant the reference's scope
+ * lists next (add+RMSNorm feeding an fp8 GEMM), with vLLM's
+ * torch.ops._C.fused_add_rms_norm_static_fp8_quant(result, input, residual, weight, scale,
+ * epsilon) argument order and the reference oracle's arithmetic up to the quantisation
+ * (src/inference_performance_lab/kernels/reference.py:18-21).
+ */
+IPL_API ipl_status ipl_fused_add_rms_norm_static_fp8_quant(void* output, const void* input, void* residual,
+                                                           const void* weight, const float* scale, int64_t rows,
+                                                           int64_t hidden_size, double epsilon, void* stream);
+
+/*
  * SiLU-and-multiply: output[r, c] = bf16(silu(fp32(input[r, c])) * fp32(input[r, I + c])),
  * I = intermediate_size, input [rows, 2*I] and output [rows, I], both contiguous. Any width and
  * alignment is accepted; aligned widths take the vector path. rows * I == 0 is a no-op.
@@ -130,6 +150,9 @@ IPL_API const char* ipl_fused_add_rms_norm_plan(const void* x, const void* resid
                                         int64_t rows, int64_t hidden_size);
 IPL_API const char* ipl_rms_norm_plan(const void* output, const void* input, const void* weight,
                                       int64_t rows, int64_t hidden_size);
+IPL_API const char* ipl_fused_add_rms_norm_static_fp8_quant_plan(const void* output, const void* input,
+                                                                 const void* residual, const void* weight,
+                                                                 int64_t rows, int64_t hidden_size);
 IPL_API const char* ipl_silu_and_mul_plan(const void* output, const void* input, int64_t rows,
                                   int64_t intermediate_size);
 

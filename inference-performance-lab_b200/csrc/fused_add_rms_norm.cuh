@@ -36,6 +36,15 @@
 
 namespace ipl {
 
+// What a row kernel computes.
+//   kModeFused:    residual = bf16(x + residual); x = bf16(norm)           (the reference op)
+//   kModePlain:    out = bf16(norm(x))                                     (RMSNorm, no residual)
+//   kModeFusedFp8: residual = bf16(x + residual); out8 = e4m3(norm / scale) (x read only)
+// norm = (v * rsqrt(mean(v^2) + eps)) * gamma with v = fp32 sum (or fp32 x).
+constexpr int kModeFused = 0;
+constexpr int kModePlain = 1;
+constexpr int kModeFusedFp8 = 2;
+
 constexpr int kStagedConsumerWarps = 16;
 constexpr int kStagedThreads = (kStagedConsumerWarps + 1) * kWarpSize;  // + 1 producer warp
 constexpr int kStagedMaxStages = 32;
@@ -47,6 +56,8 @@ struct StagedParams {
     uint16_t* x;          // input rows (and the normalised output of the fused op)
     uint16_t* residual;   // fused op: residual rows, updated in place; plain RMSNorm: unused
     uint16_t* out;        // normalised output rows (== x for the fused op)
+    uint8_t* out8;        // fp8 (e4m3) output rows of kModeFusedFp8
+    const float* scale;   // kModeFusedFp8: device scalar, output = norm / *scale
     const uint16_t* weight;
     int64_t rows;
     int hidden;
@@ -157,6 +168,22 @@ __device__ __forceinline__ uint32_t gamma_offset(int i, uint32_t plane_bytes) {
     return 16u * static_cast<uint32_t>(i >> 3) + ((i & 4) ? plane_bytes : 0u) + 4u * static_cast<uint32_t>(i & 3);
 }
 
+// 8 normalised values -> 8 e4m3 bytes (saturating, round to nearest even), stored at dst: one
+// 8-byte store when the chunk is whole and dst is 8-byte aligned, element by element otherwise.
+__device__ __forceinline__ void store_fp8_chunk(uint8_t* dst, const Pairs4& v, bool full, int first, int hidden) {
+    const uint32_t w0 = f32x2_to_e4m3x2(v.v[0]) | (f32x2_to_e4m3x2(v.v[1]) << 16);
+    const uint32_t w1 = f32x2_to_e4m3x2(v.v[2]) | (f32x2_to_e4m3x2(v.v[3]) << 16);
+    if (full && (reinterpret_cast<uintptr_t>(dst) & 7u) == 0) {
+        st_v2(dst, w0, w1);
+        return;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const int column = first + e;
+        if (column >= 0 && column < hidden) dst[e] = static_cast<uint8_t>(((e < 4 ? w0 : w1) >> (8 * (e & 3))) & 0xffu);
+    }
+}
+
 // fp32 gamma of chunk k as four pairs. With shift 0 two 16-byte loads (one per plane); otherwise
 // (rows whose phase differs from row 0's, only when H % 8 != 0) gathered element by element,
 // zero outside the staged span.
@@ -179,10 +206,12 @@ __device__ __forceinline__ Pairs4 weight_chunk(uint32_t wf_base, uint32_t plane_
     return w;
 }
 
-// kResidual: the fused residual add (x, residual -> residual = bf16(x + r), x = norm) when
-// true; plain RMSNorm (x -> out = norm(x)) when false. out must share x's offset modulo 16.
-template <int kWarpsPerRow, bool kResidual>
+// kMode as above. out (bf16 modes) must share x's offset modulo 16; the fp8 mode is planned only
+// for 16-byte aligned rows with H % 8 == 0, so every fp8 chunk store is whole and 8-byte aligned.
+template <int kWarpsPerRow, int kMode>
 __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const StagedParams p) {
+    constexpr bool kResidual = kMode != kModePlain;
+    constexpr bool kFp8 = kMode == kModeFusedFp8;
     static_assert(kStagedConsumerWarps % kWarpsPerRow == 0, "groups must tile the consumer warps");
     constexpr int kGroups = kStagedConsumerWarps / kWarpsPerRow;
     constexpr int kGroupThreads = kWarpsPerRow * kWarpSize;
@@ -283,6 +312,8 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
     }
     grid_launch_dependents();
     const uint32_t wf_base = smem_base + layout.weight_f32_offset;
+    const float scale_inv = kFp8 ? 1.0f / *p.scale : 1.0f;
+    const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
 
     const int group = warp / kWarpsPerRow;
     const int warp_in_group = warp % kWarpsPerRow;
@@ -404,7 +435,13 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
                     Pairs4 v;
 #pragma unroll
                     for (int i = 0; i < 4; ++i) v.v[i] = f32x2_mul(f32x2_mul(vs[u].v[i], inv2), ws[u].v[i]);
-                    store_chunk(obase + 8 * k, chunk_to_bf16(v), full, first, p.hidden);
+                    if constexpr (kFp8) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) v.v[i] = f32x2_mul(v.v[i], scale_inv2);
+                        store_fp8_chunk(p.out8 + row * p.hidden + first, v, full, first, p.hidden);
+                    } else {
+                        store_chunk(obase + 8 * k, chunk_to_bf16(v), full, first, p.hidden);
+                    }
                 }
             }
         }
@@ -433,14 +470,18 @@ struct WarpRowParams {
     uint16_t* x;
     uint16_t* residual;
     uint16_t* out;
+    uint8_t* out8;
+    const float* scale;
     const uint16_t* weight;
     int64_t rows;
     int hidden;
     float epsilon;
 };
 
-template <int kChunks, bool kResidual>
+template <int kChunks, int kMode>
 __global__ void __launch_bounds__(kWarpRowThreads) rmsnorm_warp_kernel(const WarpRowParams p) {
+    constexpr bool kResidual = kMode != kModePlain;
+    constexpr bool kFp8 = kMode == kModeFusedFp8;
     extern __shared__ __align__(128) unsigned char smem[];  // fp32 gamma, two planes
     const int chunks = p.hidden >> 3;
     const uint32_t plane = static_cast<uint32_t>(chunks) * 16u;
@@ -451,6 +492,8 @@ __global__ void __launch_bounds__(kWarpRowThreads) rmsnorm_warp_kernel(const War
     }
     __syncthreads();
     grid_launch_dependents();
+    const float scale_inv = kFp8 ? 1.0f / *p.scale : 1.0f;
+    const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
 
     const int lane = threadIdx.x % kWarpSize;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (kWarpRowThreads / kWarpSize);
@@ -499,7 +542,13 @@ __global__ void __launch_bounds__(kWarpRowThreads) rmsnorm_warp_kernel(const War
                 lds_pairs(gamma_base + plane + 16u * c, w.v[2], w.v[3]);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) v[i].v[e] = f32x2_mul(f32x2_mul(v[i].v[e], inv2), w.v[e]);
-                st_v4(orow + 8 * c, chunk_to_bf16(v[i]));
+                if constexpr (kFp8) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) v[i].v[e] = f32x2_mul(v[i].v[e], scale_inv2);
+                    store_fp8_chunk(p.out8 + row * p.hidden + 8 * c, v[i], true, 8 * c, p.hidden);
+                } else {
+                    st_v4(orow + 8 * c, chunk_to_bf16(v[i]));
+                }
             }
         }
     }
@@ -521,19 +570,30 @@ __device__ __forceinline__ float block_sum_rowwise(float value, float* partials)
 }
 
 // kCached: v kept in registers (H <= kRowwiseThreads * kRowwiseCachedPerThread); otherwise the
-// row is read twice. kResidual as for the staged kernel; out may alias x.
-template <bool kCached, bool kResidual>
+// row is read twice. kMode as for the staged kernel; out may alias x.
+template <bool kCached, int kMode>
 __global__ void __launch_bounds__(kRowwiseThreads) rmsnorm_rowwise_kernel(
-    const uint16_t* x, uint16_t* residual, uint16_t* out, const uint16_t* __restrict__ weight, int64_t rows,
-    int hidden, float epsilon) {
+    const uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8, const float* scale,
+    const uint16_t* __restrict__ weight, int64_t rows, int hidden, float epsilon) {
+    constexpr bool kResidual = kMode != kModePlain;
+    constexpr bool kFp8 = kMode == kModeFusedFp8;
     __shared__ float partials[kRowwiseThreads / kWarpSize];
     grid_dependency_wait();
     grid_launch_dependents();
+    const float scale_inv = kFp8 ? 1.0f / *scale : 1.0f;
     const float den = static_cast<float>(hidden);
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
         const uint16_t* xr = x + row * hidden;
         uint16_t* rr = kResidual ? residual + row * hidden : nullptr;
-        uint16_t* orow = out + row * hidden;
+        uint16_t* orow = kFp8 ? nullptr : out + row * hidden;
+        uint8_t* orow8 = kFp8 ? out8 + row * hidden : nullptr;
+        auto emit = [&](int c, float normed) {
+            if constexpr (kFp8) {
+                orow8[c] = float_to_e4m3(__fmul_rn(normed, scale_inv));
+            } else {
+                orow[c] = float_to_bf16_bits(normed);
+            }
+        };
         auto load_v = [&](int c) {
             const float xv = bf16_bits_to_float(xr[c]);
             if constexpr (kResidual) {
@@ -568,16 +628,13 @@ __global__ void __launch_bounds__(kRowwiseThreads) rmsnorm_rowwise_kernel(
 #pragma unroll
             for (int i = 0; i < kRowwiseCachedPerThread; ++i) {
                 const int c = threadIdx.x + i * kRowwiseThreads;
-                if (c < hidden) {
-                    orow[c] = float_to_bf16_bits(
-                        __fmul_rn(__fmul_rn(cache[i], inv), bf16_bits_to_float(weight[c])));
-                }
+                if (c < hidden) emit(c, __fmul_rn(__fmul_rn(cache[i], inv), bf16_bits_to_float(weight[c])));
             }
         } else {
             for (int c = threadIdx.x; c < hidden; c += kRowwiseThreads) {
                 const float v = load_v(c);
                 if constexpr (kResidual) rr[c] = float_to_bf16_bits(v);
-                orow[c] = float_to_bf16_bits(__fmul_rn(__fmul_rn(v, inv), bf16_bits_to_float(weight[c])));
+                emit(c, __fmul_rn(__fmul_rn(v, inv), bf16_bits_to_float(weight[c])));
             }
         }
     }

@@ -93,31 +93,33 @@ struct RmsPlan {
 };
 
 // Kernel names as reported by the plan queries (static strings).
-const char* rms_kernel_name(const RmsPlan& plan, bool residual) {
-    static const char* const kStagedNames[2][5] = {
+const char* rms_kernel_name(const RmsPlan& plan, int mode) {
+    static const char* const kStagedNames[3][5] = {
+        {"rmsnorm_staged_kernel<1>", "rmsnorm_staged_kernel<2>", "rmsnorm_staged_kernel<4>",
+         "rmsnorm_staged_kernel<8>", "rmsnorm_staged_kernel<16>"},
         {"rmsnorm_staged_kernel<1, plain>", "rmsnorm_staged_kernel<2, plain>", "rmsnorm_staged_kernel<4, plain>",
          "rmsnorm_staged_kernel<8, plain>", "rmsnorm_staged_kernel<16, plain>"},
-        {"rmsnorm_staged_kernel<1>", "rmsnorm_staged_kernel<2>", "rmsnorm_staged_kernel<4>",
-         "rmsnorm_staged_kernel<8>", "rmsnorm_staged_kernel<16>"}};
+        {"rmsnorm_staged_kernel<1, fp8>", "rmsnorm_staged_kernel<2, fp8>", "rmsnorm_staged_kernel<4, fp8>",
+         "rmsnorm_staged_kernel<8, fp8>", "rmsnorm_staged_kernel<16, fp8>"}};
+    static const char* const kWarpNames[3][3] = {
+        {"rmsnorm_warp_kernel<1>", "rmsnorm_warp_kernel<2>", "rmsnorm_warp_kernel<4>"},
+        {"rmsnorm_warp_kernel<1, plain>", "rmsnorm_warp_kernel<2, plain>", "rmsnorm_warp_kernel<4, plain>"},
+        {"rmsnorm_warp_kernel<1, fp8>", "rmsnorm_warp_kernel<2, fp8>", "rmsnorm_warp_kernel<4, fp8>"}};
+    static const char* const kRowwiseNames[3][2] = {
+        {"rmsnorm_rowwise_kernel<cached>", "rmsnorm_rowwise_kernel<two-pass>"},
+        {"rmsnorm_rowwise_kernel<cached, plain>", "rmsnorm_rowwise_kernel<two-pass, plain>"},
+        {"rmsnorm_rowwise_kernel<cached, fp8>", "rmsnorm_rowwise_kernel<two-pass, fp8>"}};
+    int i = 0;
     switch (plan.family) {
         case RmsFamily::kNone: return "none";
-        case RmsFamily::kStaged: {
-            int i = 0;
+        case RmsFamily::kStaged:
             while ((1 << i) < plan.warps_per_row) ++i;
-            return kStagedNames[residual ? 1 : 0][i];
-        }
-        case RmsFamily::kWarpRow: {
-            static const char* const kWarpNames[2][3] = {
-                {"rmsnorm_warp_kernel<1, plain>", "rmsnorm_warp_kernel<2, plain>", "rmsnorm_warp_kernel<4, plain>"},
-                {"rmsnorm_warp_kernel<1>", "rmsnorm_warp_kernel<2>", "rmsnorm_warp_kernel<4>"}};
-            int i = 0;
+            return kStagedNames[mode][i];
+        case RmsFamily::kWarpRow:
             while ((1 << i) < plan.chunks_per_lane) ++i;
-            return kWarpNames[residual ? 1 : 0][i];
-        }
-        case RmsFamily::kRowwiseCached:
-            return residual ? "rmsnorm_rowwise_kernel<cached>" : "rmsnorm_rowwise_kernel<cached, plain>";
-        case RmsFamily::kRowwiseTwoPass:
-            return residual ? "rmsnorm_rowwise_kernel<two-pass>" : "rmsnorm_rowwise_kernel<two-pass, plain>";
+            return kWarpNames[mode][i];
+        case RmsFamily::kRowwiseCached: return kRowwiseNames[mode][0];
+        case RmsFamily::kRowwiseTwoPass: return kRowwiseNames[mode][1];
     }
     return "invalid";
 }
@@ -143,14 +145,19 @@ ipl_status check_rms_args(const void* x, const void* other, const void* weight, 
     return IPL_SUCCESS;
 }
 
-// Pure function of the arguments and two device limits. `other` is the residual (fused op) or
-// the output (plain op); either must share x's offset modulo 16 bytes for the staged kernel.
-RmsPlan plan_rms(const void* x, const void* other, int64_t rows, int64_t hidden, bool residual, int sm_count,
-                 int smem_limit) {
+// Pure function of the arguments and two device limits. `other` is the residual (fused modes) or
+// the output (plain mode); either must share x's offset modulo 16 bytes for the staged kernel.
+// `out8` is the fp8 output of kModeFusedFp8, whose vector paths need 16-byte aligned rows
+// (H % 8 == 0) and an 8-byte aligned output.
+RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t rows, int64_t hidden, int mode,
+                 int sm_count, int smem_limit) {
     RmsPlan plan;
     if (rows == 0) return plan;
+    const bool residual = mode != kModePlain;
     const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
     const uintptr_t oa = reinterpret_cast<uintptr_t>(other);
+    const bool fp8_vector_ok = mode != kModeFusedFp8 ||
+                               (hidden % 8 == 0 && (xa & 15u) == 0 && (reinterpret_cast<uintptr_t>(out8) & 7u) == 0);
     const int chunks_max = static_cast<int>((hidden + 7) / 8 + 1);
     const int stage_bytes = (residual ? 2 : 1) * chunks_max * 16;
     const int row_phase = static_cast<int>((xa & 15u) >> 1);
@@ -160,7 +167,7 @@ RmsPlan plan_rms(const void* x, const void* other, int64_t rows, int64_t hidden,
     if (max_stages > kStagedMaxStages) max_stages = kStagedMaxStages;
 
     // Short aligned rows: a warp per row, values in registers.
-    if (hidden % 8 == 0 && hidden <= kWarpRowMaxHidden && ((xa | oa) & 15u) == 0) {
+    if (hidden % 8 == 0 && hidden <= kWarpRowMaxHidden && ((xa | oa) & 15u) == 0 && fp8_vector_ok) {
         const int64_t per_lane = (hidden / 8 + kWarpSize - 1) / kWarpSize;
         plan.family = RmsFamily::kWarpRow;
         plan.chunks_per_lane = per_lane <= 1 ? 1 : per_lane <= 2 ? 2 : 4;
@@ -171,7 +178,7 @@ RmsPlan plan_rms(const void* x, const void* other, int64_t rows, int64_t hidden,
         plan.smem = static_cast<size_t>(hidden) * 4u;
         return plan;
     }
-    if ((xa & 15u) == (oa & 15u) && max_stages >= 2) {
+    if ((xa & 15u) == (oa & 15u) && max_stages >= 2 && fp8_vector_ok) {
         const int grid = static_cast<int>(rows < sm_count ? rows : sm_count);
         const int64_t rows_per_cta = (rows + grid - 1) / grid;
         // Ring depth S and consumer groups G (W = 16 / G warps per row), from a sweep of both on
@@ -221,71 +228,77 @@ RmsPlan plan_rms(const void* x, const void* other, int64_t rows, int64_t hidden,
     return plan;
 }
 
-template <int W, bool kResidual>
+const char* mode_label(int mode) {
+    return mode == kModeFused ? "fused RMSNorm" : mode == kModePlain ? "RMSNorm" : "fused RMSNorm fp8";
+}
+
+template <int W, int kMode>
 ipl_status launch_staged(const RmsPlan& plan, DeviceInfo* info, cudaStream_t stream) {
-    auto kernel = rmsnorm_staged_kernel<W, kResidual>;
+    auto kernel = rmsnorm_staged_kernel<W, kMode>;
     int bit = 0;
     while ((1 << bit) < W) ++bit;
-    bit += kResidual ? 0 : 8;
+    bit += 8 * kMode;
     if (!(info->smem_configured.load(std::memory_order_acquire) & (1u << bit))) {
         const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                      info->max_smem_optin.load());
         if (err != cudaSuccess) {
-            return fail(IPL_ERROR_CUDA, "%s kernel setup failed: %s", kResidual ? "fused RMSNorm" : "RMSNorm",
-                        cudaGetErrorString(err));
+            return fail(IPL_ERROR_CUDA, "%s kernel setup failed: %s", mode_label(kMode), cudaGetErrorString(err));
         }
         info->smem_configured.fetch_or(1u << bit, std::memory_order_acq_rel);
     }
     const cudaError_t err = launch(kernel, plan.grid, kStagedThreads, plan.smem, stream, plan.staged);
     if (err != cudaSuccess) {
-        return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", kResidual ? "fused RMSNorm" : "RMSNorm",
-                    cudaGetErrorString(err));
+        return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
     }
     return IPL_SUCCESS;
 }
 
-template <bool kResidual>
-ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, const uint16_t* weight, int64_t rows,
-                   int64_t hidden, double epsilon, cudaStream_t stream) {
+template <int kMode>
+ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8, const float* scale,
+                   const uint16_t* weight, int64_t rows, int64_t hidden, double epsilon, cudaStream_t stream) {
+    constexpr bool kResidual = kMode != kModePlain;
     int device = 0;
     DeviceInfo* info = nullptr;
     ipl_status st = current_device(&device, &info);
     if (st != IPL_SUCCESS) return st;
-    RmsPlan plan = plan_rms(x, kResidual ? static_cast<const void*>(residual) : static_cast<const void*>(out), rows,
-                            hidden, kResidual, info->sm_count.load(std::memory_order_relaxed),
+    RmsPlan plan = plan_rms(x, kResidual ? static_cast<const void*>(residual) : static_cast<const void*>(out), out8,
+                            rows, hidden, kMode, info->sm_count.load(std::memory_order_relaxed),
                             info->max_smem_optin.load(std::memory_order_relaxed));
     plan.staged.x = x;
     plan.staged.residual = residual;
     plan.staged.out = out;
+    plan.staged.out8 = out8;
+    plan.staged.scale = scale;
     plan.staged.weight = weight;
     plan.staged.epsilon = static_cast<float>(epsilon);
     switch (plan.family) {
         case RmsFamily::kStaged:
             switch (plan.warps_per_row) {
-                case 1: return launch_staged<1, kResidual>(plan, info, stream);
-                case 2: return launch_staged<2, kResidual>(plan, info, stream);
-                case 4: return launch_staged<4, kResidual>(plan, info, stream);
-                case 8: return launch_staged<8, kResidual>(plan, info, stream);
-                default: return launch_staged<16, kResidual>(plan, info, stream);
+                case 1: return launch_staged<1, kMode>(plan, info, stream);
+                case 2: return launch_staged<2, kMode>(plan, info, stream);
+                case 4: return launch_staged<4, kMode>(plan, info, stream);
+                case 8: return launch_staged<8, kMode>(plan, info, stream);
+                default: return launch_staged<16, kMode>(plan, info, stream);
             }
         case RmsFamily::kWarpRow: {
             WarpRowParams w;
             w.x = x;
             w.residual = residual;
             w.out = out;
+            w.out8 = out8;
+            w.scale = scale;
             w.weight = weight;
             w.rows = rows;
             w.hidden = static_cast<int>(hidden);
             w.epsilon = plan.staged.epsilon;
             cudaError_t err = cudaSuccess;
             switch (plan.chunks_per_lane) {
-                case 1: err = launch(rmsnorm_warp_kernel<1, kResidual>, plan.grid, kWarpRowThreads, plan.smem, stream, w); break;
-                case 2: err = launch(rmsnorm_warp_kernel<2, kResidual>, plan.grid, kWarpRowThreads, plan.smem, stream, w); break;
-                default: err = launch(rmsnorm_warp_kernel<4, kResidual>, plan.grid, kWarpRowThreads, plan.smem, stream, w); break;
+                case 1: err = launch(rmsnorm_warp_kernel<1, kMode>, plan.grid, kWarpRowThreads, plan.smem, stream, w); break;
+                case 2: err = launch(rmsnorm_warp_kernel<2, kMode>, plan.grid, kWarpRowThreads, plan.smem, stream, w); break;
+                default: err = launch(rmsnorm_warp_kernel<4, kMode>, plan.grid, kWarpRowThreads, plan.smem, stream, w); break;
             }
             if (err != cudaSuccess) {
-                return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", kResidual ? "fused RMSNorm" : "RMSNorm",
-                            cudaGetErrorString(err));
+                return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
             }
             return IPL_SUCCESS;
         }
@@ -293,15 +306,14 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, const uint16_
         case RmsFamily::kRowwiseTwoPass: {
             const cudaError_t err =
                 plan.family == RmsFamily::kRowwiseCached
-                    ? launch(rmsnorm_rowwise_kernel<true, kResidual>, plan.grid, kRowwiseThreads, 0, stream,
-                             static_cast<const uint16_t*>(x), residual, out, weight, rows, static_cast<int>(hidden),
-                             plan.staged.epsilon)
-                    : launch(rmsnorm_rowwise_kernel<false, kResidual>, plan.grid, kRowwiseThreads, 0, stream,
-                             static_cast<const uint16_t*>(x), residual, out, weight, rows, static_cast<int>(hidden),
-                             plan.staged.epsilon);
+                    ? launch(rmsnorm_rowwise_kernel<true, kMode>, plan.grid, kRowwiseThreads, 0, stream,
+                             static_cast<const uint16_t*>(x), residual, out, out8, scale, weight, rows,
+                             static_cast<int>(hidden), plan.staged.epsilon)
+                    : launch(rmsnorm_rowwise_kernel<false, kMode>, plan.grid, kRowwiseThreads, 0, stream,
+                             static_cast<const uint16_t*>(x), residual, out, out8, scale, weight, rows,
+                             static_cast<int>(hidden), plan.staged.epsilon);
             if (err != cudaSuccess) {
-                return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", kResidual ? "fused RMSNorm" : "RMSNorm",
-                            cudaGetErrorString(err));
+                return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
             }
             return IPL_SUCCESS;
         }
@@ -433,18 +445,35 @@ ipl_status ipl_fused_add_rms_norm_bf16(void* x, void* residual, const void* weig
                                        int64_t hidden_size, double epsilon, void* stream) {
     const ipl_status st = check_rms_args(x, residual, weight, rows, hidden_size, epsilon, true);
     if (st != IPL_SUCCESS || rows == 0) return st;
-    return run_rms<true>(static_cast<uint16_t*>(x), static_cast<uint16_t*>(residual), static_cast<uint16_t*>(x),
-                         static_cast<const uint16_t*>(weight), rows, hidden_size, epsilon,
-                         static_cast<cudaStream_t>(stream));
+    return run_rms<kModeFused>(static_cast<uint16_t*>(x), static_cast<uint16_t*>(residual), static_cast<uint16_t*>(x),
+                               nullptr, nullptr, static_cast<const uint16_t*>(weight), rows, hidden_size, epsilon,
+                               static_cast<cudaStream_t>(stream));
 }
 
 ipl_status ipl_rms_norm_bf16(void* output, const void* input, const void* weight, int64_t rows,
                              int64_t hidden_size, double epsilon, void* stream) {
     const ipl_status st = check_rms_args(input, output, weight, rows, hidden_size, epsilon, false);
     if (st != IPL_SUCCESS || rows == 0) return st;
-    return run_rms<false>(const_cast<uint16_t*>(static_cast<const uint16_t*>(input)), nullptr,
-                          static_cast<uint16_t*>(output), static_cast<const uint16_t*>(weight), rows, hidden_size,
-                          epsilon, static_cast<cudaStream_t>(stream));
+    return run_rms<kModePlain>(const_cast<uint16_t*>(static_cast<const uint16_t*>(input)), nullptr,
+                               static_cast<uint16_t*>(output), nullptr, nullptr, static_cast<const uint16_t*>(weight),
+                               rows, hidden_size, epsilon, static_cast<cudaStream_t>(stream));
+}
+
+ipl_status ipl_fused_add_rms_norm_static_fp8_quant(void* output, const void* input, void* residual,
+                                                   const void* weight, const float* scale, int64_t rows,
+                                                   int64_t hidden_size, double epsilon, void* stream) {
+    ipl_status st = check_rms_args(input, residual, weight, rows, hidden_size, epsilon, true);
+    if (st != IPL_SUCCESS || rows == 0) return st;
+    if (output == nullptr || scale == nullptr) {
+        return fail(IPL_ERROR_INVALID_VALUE, "output and scale must be non-null");
+    }
+    if (reinterpret_cast<uintptr_t>(scale) & 3u) {
+        return fail(IPL_ERROR_INVALID_VALUE, "scale must be 4-byte aligned");
+    }
+    uint16_t* x = const_cast<uint16_t*>(static_cast<const uint16_t*>(input));
+    return run_rms<kModeFusedFp8>(x, static_cast<uint16_t*>(residual), x, static_cast<uint8_t*>(output), scale,
+                                  static_cast<const uint16_t*>(weight), rows, hidden_size, epsilon,
+                                  static_cast<cudaStream_t>(stream));
 }
 
 ipl_status ipl_silu_and_mul_bf16(void* output, const void* input, int64_t rows, int64_t intermediate_size,
@@ -505,13 +534,22 @@ const char* ipl_fused_add_rms_norm_plan(const void* x, const void* residual, con
                                         int64_t hidden_size) {
     if (check_rms_args(x, residual, weight, rows, hidden_size, 1.0, true) != IPL_SUCCESS) return "invalid";
     // B200 limits: 148 SMs, 232448 bytes of opt-in shared memory per block.
-    return rms_kernel_name(plan_rms(x, residual, rows, hidden_size, true, 148, 232448), true);
+    return rms_kernel_name(plan_rms(x, residual, nullptr, rows, hidden_size, kModeFused, 148, 232448), kModeFused);
 }
 
 const char* ipl_rms_norm_plan(const void* output, const void* input, const void* weight, int64_t rows,
                               int64_t hidden_size) {
     if (check_rms_args(input, output, weight, rows, hidden_size, 1.0, false) != IPL_SUCCESS) return "invalid";
-    return rms_kernel_name(plan_rms(input, output, rows, hidden_size, false, 148, 232448), false);
+    return rms_kernel_name(plan_rms(input, output, nullptr, rows, hidden_size, kModePlain, 148, 232448), kModePlain);
+}
+
+const char* ipl_fused_add_rms_norm_static_fp8_quant_plan(const void* output, const void* input, const void* residual,
+                                                         const void* weight, int64_t rows, int64_t hidden_size) {
+    if (check_rms_args(input, residual, weight, rows, hidden_size, 1.0, true) != IPL_SUCCESS || output == nullptr) {
+        return "invalid";
+    }
+    return rms_kernel_name(plan_rms(input, residual, output, rows, hidden_size, kModeFusedFp8, 148, 232448),
+                           kModeFusedFp8);
 }
 
 const char* ipl_silu_and_mul_plan(const void* output, const void* input, int64_t rows,

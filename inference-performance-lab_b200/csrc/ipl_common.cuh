@@ -39,6 +39,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(hi), "f"(lo));
     return packed;
 }
+// fp32 -> fp8 e4m3 (OCP E4M3FN: bias 7, max 448, no infinities), round to nearest even,
+// saturating to +-448; NaN -> 0x7F.
+__device__ __forceinline__ uint8_t float_to_e4m3(float value) {
+    uint16_t packed;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(packed) : "f"(0.0f), "f"(value));
+    return static_cast<uint8_t>(packed & 0xffu);
+}
 __device__ __forceinline__ uint16_t float_to_bf16_bits(float value) {
     return static_cast<uint16_t>(pack_bf16x2(value, 0.0f) & 0xffffu);
 }
@@ -74,6 +81,15 @@ __device__ __forceinline__ F32x2 f32x2_fma(F32x2 a, F32x2 b, F32x2 c) {
 __device__ __forceinline__ F32x2 bf16x2_widen(uint32_t packed) {
     return f32x2_make(__uint_as_float(packed << 16), __uint_as_float(packed & 0xffff0000u));
 }
+// fp32 pair -> two e4m3 bytes (low element in the low byte), saturating, round to nearest even.
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(F32x2 v) {
+    float lo, hi;
+    f32x2_split(v, lo, hi);
+    uint16_t packed;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(packed) : "f"(hi), "f"(lo));
+    return packed;
+}
+
 // fp32 pair -> bf16x2 word, round to nearest even.
 __device__ __forceinline__ uint32_t f32x2_to_bf16x2(F32x2 v) {
     float lo, hi;
@@ -119,6 +135,9 @@ __device__ __forceinline__ U32x4 ld_v4(const void* p) {
                  : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3])
                  : "l"(p));
     return r;
+}
+__device__ __forceinline__ void st_v2(void* p, uint32_t a, uint32_t b) {
+    asm volatile("st.global.v2.b32 [%0], {%1,%2};" ::"l"(p), "r"(a), "r"(b) : "memory");
 }
 __device__ __forceinline__ void st_v4(void* p, const U32x4& r) {
     asm volatile("st.global.v4.b32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(r.v[0]), "r"(r.v[1]),

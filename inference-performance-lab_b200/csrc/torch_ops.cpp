@@ -137,6 +137,43 @@ void rms_norm_cuda(ts::Tensor& output, const ts::Tensor& input, const ts::Tensor
                                      rows, hidden_size, epsilon, stream));
 }
 
+void fused_add_rms_norm_static_fp8_quant_cuda(ts::Tensor& result, const ts::Tensor& input, ts::Tensor& residual,
+                                              const ts::Tensor& weight, const ts::Tensor& scale, double epsilon) {
+    STD_TORCH_CHECK(result.is_cuda() && input.is_cuda() && residual.is_cuda() && weight.is_cuda() && scale.is_cuda(),
+                    "result, input, residual, weight, and scale must be CUDA tensors");
+    STD_TORCH_CHECK(result.scalar_type() == torch::headeronly::ScalarType::Float8_e4m3fn,
+                    "result must use float8_e4m3fn");
+    STD_TORCH_CHECK(input.scalar_type() == torch::headeronly::ScalarType::BFloat16 &&
+                        residual.scalar_type() == torch::headeronly::ScalarType::BFloat16 &&
+                        weight.scalar_type() == torch::headeronly::ScalarType::BFloat16,
+                    "input, residual, and weight must use bfloat16");
+    STD_TORCH_CHECK(scale.scalar_type() == torch::headeronly::ScalarType::Float && scale.numel() == 1,
+                    "scale must be a single float32");
+    STD_TORCH_CHECK(result.is_contiguous() && input.is_contiguous() && residual.is_contiguous() &&
+                        weight.is_contiguous(),
+                    "result, input, residual, and weight must be contiguous");
+    STD_TORCH_CHECK(input.sizes().equals(residual.sizes()) && input.sizes().equals(result.sizes()),
+                    "result, input, and residual must have identical shapes");
+    STD_TORCH_CHECK(input.device() == residual.device() && input.device() == weight.device() &&
+                        input.device() == result.device() && input.device() == scale.device(),
+                    "all tensors must be on the same device");
+    STD_TORCH_CHECK(input.dim() >= 1, "input must have at least one dimension");
+    STD_TORCH_CHECK(weight.dim() == 1, "weight must be one-dimensional");
+    STD_TORCH_CHECK(weight.size(0) == input.size(-1), "weight must match the final tensor dimension");
+    STD_TORCH_CHECK(epsilon > 0.0, "epsilon must be positive");
+    if (input.numel() == 0) {
+        return;
+    }
+    const int64_t hidden_size = input.size(-1);
+    const int64_t rows = input.numel() / hidden_size;
+    const int32_t device = input.get_device_index();
+    const ts::accelerator::DeviceGuard device_guard(device);
+    void* stream = current_stream(device);
+    raise_on_error(ipl_fused_add_rms_norm_static_fp8_quant(
+        result.mutable_data_ptr(), input.const_data_ptr(), residual.mutable_data_ptr(), weight.const_data_ptr(),
+        static_cast<const float*>(scale.const_data_ptr()), rows, hidden_size, epsilon, stream));
+}
+
 void silu_and_mul_cuda(ts::Tensor& output, const ts::Tensor& input) { run_silu(output, input, false); }
 
 void silu_and_mul_packed_cuda(ts::Tensor& output, const ts::Tensor& input) { run_silu(output, input, true); }
@@ -147,6 +184,10 @@ STABLE_TORCH_LIBRARY(inference_performance_lab, library) {
     library.def("silu_and_mul_packed(Tensor(a!) output, Tensor input) -> ()");
     // Not in the reference library: plain RMSNorm (vLLM's _C.rms_norm argument order).
     library.def("rms_norm(Tensor(a!) output, Tensor input, Tensor weight, float epsilon) -> ()");
+    // Not in the reference library: add+RMSNorm with a static fp8 output (vLLM's argument order).
+    library.def(
+        "fused_add_rms_norm_static_fp8_quant(Tensor(a!) result, Tensor input, Tensor(b!) residual, "
+        "Tensor weight, Tensor scale, float epsilon) -> ()");
 }
 
 STABLE_TORCH_LIBRARY_IMPL(inference_performance_lab, CUDA, library) {
@@ -154,4 +195,5 @@ STABLE_TORCH_LIBRARY_IMPL(inference_performance_lab, CUDA, library) {
     library.impl("silu_and_mul", TORCH_BOX(&silu_and_mul_cuda));
     library.impl("silu_and_mul_packed", TORCH_BOX(&silu_and_mul_packed_cuda));
     library.impl("rms_norm", TORCH_BOX(&rms_norm_cuda));
+    library.impl("fused_add_rms_norm_static_fp8_quant", TORCH_BOX(&fused_add_rms_norm_static_fp8_quant_cuda));
 }

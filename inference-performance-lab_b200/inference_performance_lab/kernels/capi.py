@@ -44,6 +44,20 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             ctypes.c_void_p,
         ],
     ),
+    "ipl_fused_add_rms_norm_static_fp8_quant": (
+        ctypes.c_int,
+        [
+            ctypes.c_void_p,
+            ctypes.c_void_p,
+            ctypes.c_void_p,
+            ctypes.c_void_p,
+            ctypes.c_void_p,
+            ctypes.c_int64,
+            ctypes.c_int64,
+            ctypes.c_double,
+            ctypes.c_void_p,
+        ],
+    ),
     "ipl_silu_and_mul_bf16": (
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p],
@@ -64,6 +78,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ipl_rms_norm_plan": (
         ctypes.c_char_p,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64],
+    ),
+    "ipl_fused_add_rms_norm_static_fp8_quant_plan": (
+        ctypes.c_char_p,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64],
     ),
     "ipl_silu_and_mul_plan": (
         ctypes.c_char_p,
@@ -127,6 +145,24 @@ def rms_norm(
     )
 
 
+def fused_add_rms_norm_static_fp8_quant(
+    output_ptr: int,
+    input_ptr: int,
+    residual_ptr: int,
+    weight_ptr: int,
+    scale_ptr: int,
+    rows: int,
+    hidden_size: int,
+    epsilon: float,
+    stream: int = 0,
+) -> None:
+    _check(
+        library().ipl_fused_add_rms_norm_static_fp8_quant(
+            output_ptr, input_ptr, residual_ptr, weight_ptr, scale_ptr, rows, hidden_size, epsilon, stream
+        )
+    )
+
+
 def silu_and_mul(
     output_ptr: int, input_ptr: int, rows: int, intermediate_size: int, stream: int = 0
 ) -> None:
@@ -163,6 +199,14 @@ def fused_add_rms_norm_plan(
 
 def rms_norm_plan(output_ptr: int, input_ptr: int, weight_ptr: int, rows: int, hidden_size: int) -> str:
     return library().ipl_rms_norm_plan(output_ptr, input_ptr, weight_ptr, rows, hidden_size).decode()
+
+
+def fused_add_rms_norm_static_fp8_quant_plan(
+    output_ptr: int, input_ptr: int, residual_ptr: int, weight_ptr: int, rows: int, hidden_size: int
+) -> str:
+    return library().ipl_fused_add_rms_norm_static_fp8_quant_plan(
+        output_ptr, input_ptr, residual_ptr, weight_ptr, rows, hidden_size
+    ).decode()
 
 
 def silu_and_mul_plan(output_ptr: int, input_ptr: int, rows: int, intermediate_size: int) -> str:

@@ -75,6 +75,21 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, epsilon: float) -> torch.Ten
     return output
 
 
+def fused_add_rms_norm_static_fp8_quant(
+    x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor, epsilon: float
+) -> torch.Tensor:
+    """``residual := x + residual`` in place; returns ``e4m3(rmsnorm(x + residual) * weight / scale)``
+    (x is not modified; not in the reference library)."""
+    load_extension()
+
+    output = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    torch.ops.inference_performance_lab.fused_add_rms_norm_static_fp8_quant(
+        output, x, residual, weight, scale, epsilon
+    )
+
+    return output
+
+
 def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
     """``silu(x[..., :I]) * x[..., I:]`` into a new ``[..., I]`` tensor (any width/alignment)."""
     load_extension()

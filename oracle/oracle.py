@@ -49,6 +49,13 @@ def _lib() -> ctypes.CDLL:
     lib.oracle_rms_norm_bf16.argtypes = [_U16P, _U16P, ctypes.c_int64, ctypes.c_int64, ctypes.c_double, _U16P]
     lib.oracle_silu_and_mul_bf16.restype = None
     lib.oracle_silu_and_mul_bf16.argtypes = [_U16P, ctypes.c_int64, ctypes.c_int64, _U16P]
+    lib.oracle_fused_add_rms_norm_static_fp8_quant.restype = ctypes.c_int
+    lib.oracle_fused_add_rms_norm_static_fp8_quant.argtypes = [
+        _U16P, _U16P, _U16P, ctypes.c_int64, ctypes.c_int64, ctypes.c_double, ctypes.c_float,
+        ctypes.POINTER(ctypes.c_uint8), _U16P,
+    ]
+    lib.oracle_f32_to_e4m3.restype = ctypes.c_uint8
+    lib.oracle_f32_to_e4m3.argtypes = [ctypes.c_float]
     lib.oracle_f32_to_bf16.restype = ctypes.c_uint16
     lib.oracle_f32_to_bf16.argtypes = [ctypes.c_float]
     return lib
@@ -85,6 +92,33 @@ def c_fused_add_rms_norm(
         if status != 0:
             raise MemoryError("oracle scratch allocation failed")
     return out, res
+
+
+def c_fused_add_rms_norm_static_fp8_quant(
+    x: np.ndarray, residual: np.ndarray, weight: np.ndarray, scale: float, epsilon: float
+) -> tuple[np.ndarray, np.ndarray]:
+    """(e4m3 output as uint8, residual_out as uint16 bf16 bits)."""
+    x, residual, weight = _u16(x), _u16(residual), _u16(weight)
+    if x.shape != residual.shape:
+        raise ValueError("x and residual must have identical shapes")
+    hidden = x.shape[-1]
+    rows = x.size // hidden if hidden else 0
+    out = np.empty(x.shape, dtype=np.uint8)
+    res = np.empty_like(x)
+    if rows and hidden:
+        status = _lib().oracle_fused_add_rms_norm_static_fp8_quant(
+            _ptr(x), _ptr(residual), _ptr(weight), rows, hidden, epsilon, scale,
+            out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), _ptr(res),
+        )
+        if status != 0:
+            raise MemoryError("oracle scratch allocation failed")
+    return out, res
+
+
+def c_f32_to_e4m3(values: np.ndarray) -> np.ndarray:
+    lib = _lib()
+    return np.array([lib.oracle_f32_to_e4m3(float(v)) for v in np.asarray(values, dtype=np.float32).ravel()],
+                    dtype=np.uint8)
 
 
 def c_rms_norm(x: np.ndarray, weight: np.ndarray, epsilon: float) -> np.ndarray:
@@ -151,6 +185,18 @@ def torch_rms_norm(x, weight, epsilon: float):
     v = x.float()
     inverse_rms = torch.rsqrt(v.square().mean(dim=-1, keepdim=True) + epsilon)
     return (v * inverse_rms * weight.float()).to(x.dtype)
+
+
+def torch_fused_add_rms_norm_static_fp8_quant(x, residual, weight, scale: float, epsilon: float):
+    """reference.py:18-21 in fp32, then e4m3 of product / scale saturated to +-448 (torch's own
+    float8_e4m3fn conversion, which rounds to nearest even)."""
+    import torch
+
+    summed = x.float() + residual.float()
+    inverse_rms = torch.rsqrt(summed.square().mean(dim=-1, keepdim=True) + epsilon)
+    normed = summed * inverse_rms * weight.float()
+    quantised = (normed * (1.0 / torch.tensor(scale, dtype=torch.float32))).clamp(-448.0, 448.0)
+    return quantised.to(torch.float8_e4m3fn), summed.to(residual.dtype)
 
 
 def torch_silu_and_mul(x):

@@ -88,6 +88,23 @@ def test_plain_rms_in_place_is_accepted_by_the_plan() -> None:
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 1, 8192) == "rmsnorm_staged_kernel<16, plain>"
 
 
+def test_fp8_quant_arguments_and_plans() -> None:
+    with pytest.raises(capi.IplError, match="output and scale must be non-null"):
+        capi.fused_add_rms_norm_static_fp8_quant(BASE, BASE + 4096, BASE + 8192, BASE + 12288, 0, 4, 16, 1e-6)
+    with pytest.raises(capi.IplError, match="epsilon must be positive"):
+        capi.fused_add_rms_norm_static_fp8_quant(BASE, BASE + 4096, BASE + 8192, BASE + 12288, BASE, 4, 16, 0.0)
+    plan = capi.fused_add_rms_norm_static_fp8_quant_plan
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 3584) == "rmsnorm_staged_kernel<2, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 1024) == "rmsnorm_warp_kernel<4, fp8>"
+    # fp8 vector stores need 16-byte aligned rows and an 8-byte aligned output.
+    assert plan(BASE + 4, BASE + 4098, BASE + (1 << 34) + 2, BASE + 12288, 2048, 3584).startswith(
+        "rmsnorm_rowwise_kernel"
+    )
+    assert plan(BASE + 1, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 3584).startswith(
+        "rmsnorm_rowwise_kernel"
+    )
+
+
 def test_rms_empty_batch_is_a_no_op() -> None:
     # rows == 0 returns before any device query.
     capi.fused_add_rms_norm(0, 0, 0, 0, 3584, 1e-6)

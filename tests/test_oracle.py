@@ -124,3 +124,34 @@ def test_oracle_empty_batch() -> None:
         np.zeros((0, 16), np.uint16), np.zeros((0, 16), np.uint16), np.zeros(16, np.uint16), 1e-6
     )
     assert out.shape == res.shape == (0, 16)
+
+
+def test_e4m3_conversion_matches_torch() -> None:
+    generator = torch.Generator().manual_seed(11)
+    values = torch.cat(
+        [torch.randn(5000, generator=generator) * s for s in (1e-4, 1e-2, 1.0, 30.0, 200.0)]
+        + [torch.tensor([0.0, -0.0, 448.0, -448.0, 447.9, 2.0**-9, 2.0**-10, 1.5 * 2.0**-9, 2.0**-6,
+                         0.0146484375, 240.0, 232.0, 248.0, 1.0625, 1.1875])]
+    ).clamp(-448.0, 448.0)
+    expected = values.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(oracle.c_f32_to_e4m3(values.numpy()), expected)
+    # Saturation (torch would give NaN beyond 448; the op saturates, as vLLM's does) and NaN.
+    np.testing.assert_array_equal(
+        oracle.c_f32_to_e4m3(np.array([1e6, -1e6, 464.0, np.nan], dtype=np.float32)),
+        np.array([0x7E, 0xFE, 0x7E, 0x7F], dtype=np.uint8),
+    )
+
+
+def test_fp8_quant_oracles_agree() -> None:
+    generator = torch.Generator().manual_seed(12)
+    for rows, hidden, scale in [(16, 1024, 0.05), (3, 3584, 0.01), (4, 1001, 1.0)]:
+        x = torch.randn(rows, hidden, generator=generator).to(torch.bfloat16)
+        r = torch.randn(rows, hidden, generator=generator).to(torch.bfloat16)
+        w = (torch.randn(hidden, generator=generator) * 0.1 + 1).to(torch.bfloat16)
+        c_out, c_res = oracle.c_fused_add_rms_norm_static_fp8_quant(
+            oracle.tensor_bits(x), oracle.tensor_bits(r), oracle.tensor_bits(w), scale, 1e-6
+        )
+        t_out, t_res = oracle.torch_fused_add_rms_norm_static_fp8_quant(x, r, w, scale, 1e-6)
+        np.testing.assert_array_equal(c_res, oracle.tensor_bits(t_res))
+        mismatches = int((c_out != t_out.view(torch.uint8).numpy()).sum())
+        assert mismatches <= c_out.size // 1000  # the fp32 mean may differ in its last bit
