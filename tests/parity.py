@@ -19,8 +19,12 @@ CANARY = 0x7BAD  # a finite bf16 bit pattern never produced by the tests' data p
 
 
 def require_cuda() -> None:
+    """Fail (not skip) without a GPU, and register the ops for tests that call torch.ops directly."""
     if not torch.cuda.is_available():
         pytest.fail("GPU test run without a CUDA device")
+    from inference_performance_lab.kernels.extension import load_extension
+
+    load_extension()
 
 
 class Guarded:
