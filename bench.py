@@ -55,10 +55,18 @@ WORKLOADS = {
     "rmsnorm-sharded": {"op": "fused_add_rms_norm", "rows": 262144, "hidden": 8192, "eps": 1e-5, "offset": 0,
                         "sharded": True},
     "silu": {"op": "silu_and_mul", "rows": 128, "intermediate": 18944, "std": 2.0},
+    "rmsnorm-plain": {"op": "rms_norm", "rows": 2048, "hidden": 3584, "eps": 1e-6, "offset": 0},
+    "rmsnorm-fp8": {"op": "fused_add_rms_norm_static_fp8_quant", "rows": 2048, "hidden": 3584, "eps": 1e-6,
+                    "offset": 0},
 }
 
 
 def workload_name(args, spec) -> str:
+    if spec["op"] == "rms_norm":
+        return f"rms_norm bf16 [{spec['rows']}, {spec['hidden']}] eps {spec['eps']:g} (out of place)"
+    if spec["op"] == "fused_add_rms_norm_static_fp8_quant":
+        return (f"fused_add_rms_norm_static_fp8_quant bf16 [{spec['rows']}, {spec['hidden']}] -> e4m3, "
+                f"eps {spec['eps']:g}")
     if spec["op"] == "silu_and_mul":
         return f"silu_and_mul bf16 [{spec['rows']}, {2 * spec['intermediate']}] -> [{spec['rows']}, {spec['intermediate']}]"
     name = f"fused_add_rms_norm bf16 [{spec['rows']}, {spec['hidden']}] eps {spec['eps']:g}"
@@ -70,8 +78,14 @@ def workload_name(args, spec) -> str:
 
 
 def step_bytes(spec, rows: int) -> int:
+    """Algorithmic DRAM bytes of one step: every input element read once, every output written once
+    (the weight, read once per SM, is not counted)."""
     if spec["op"] == "silu_and_mul":
         return 6 * rows * spec["intermediate"]
+    if spec["op"] == "rms_norm":
+        return 2 * spec["hidden"] * 2 * rows  # read x, write out
+    if spec["op"] == "fused_add_rms_norm_static_fp8_quant":
+        return 7 * spec["hidden"] * rows  # read x, r (4 B), write r (2 B), write e4m3 (1 B)
     return 4 * spec["hidden"] * 2 * rows
 
 
@@ -211,37 +225,132 @@ class Dist:
             self.pg.destroy_process_group()
 
 
+
 # ------------------------------------------------------------------------------------------
-# inputs
+# per-op workload: inputs, the call, the CPU reference call, host buffers for the e2e leg
 
 
-def make_rms_sets(spec, rows: int, seed: int, device, sets: int):
-    import torch
+class OpWorkload:
+    """Everything op-specific: device batches, the op call, its kernel plan, the reference's CPU
+    call on a sample, and which tensors an end-to-end step uploads and downloads."""
 
-    hidden, offset = spec["hidden"], spec.get("offset", 0)
-    generator = torch.Generator(device=device).manual_seed(seed)
-    batches = []
-    for _ in range(sets):
-        pair = []
-        for _ in range(2):
-            buf = torch.randn(rows * hidden + 8, device=device, dtype=torch.bfloat16, generator=generator)
-            pair.append(buf[offset: offset + rows * hidden].view(rows, hidden))
-        batches.append(tuple(pair))
-    weight = (torch.randn(hidden, device=device, generator=generator) * 0.1 + 1.0).to(torch.bfloat16)
-    return batches, weight
+    def __init__(self, spec) -> None:
+        self.spec = spec
+        self.op = spec["op"]
 
+    def make_sets(self, rows: int, seed: int, device, sets: int):
+        """`sets` batches (dicts of device tensors) and the tensors they share (weight, scale)."""
+        import torch
 
-def make_silu_sets(spec, seed: int, device, sets: int):
-    import torch
+        spec = self.spec
+        generator = torch.Generator(device=device).manual_seed(seed)
+        batches = []
+        if self.op == "silu_and_mul":
+            inter = spec["intermediate"]
+            for _ in range(sets):
+                x = (torch.randn(rows, 2 * inter, device=device, generator=generator) * spec["std"]).to(torch.bfloat16)
+                batches.append({"x": x, "out": torch.empty(rows, inter, device=device, dtype=torch.bfloat16)})
+            return batches, {}
+        hidden, offset = spec["hidden"], spec.get("offset", 0)
 
-    rows, inter = spec["rows"], spec["intermediate"]
-    generator = torch.Generator(device=device).manual_seed(seed)
-    batches = []
-    for _ in range(sets):
-        x = (torch.randn(rows, 2 * inter, device=device, generator=generator) * spec["std"]).to(torch.bfloat16)
-        out = torch.empty(rows, inter, device=device, dtype=torch.bfloat16)
-        batches.append((out, x))
-    return batches
+        def row_view(buf):
+            return buf[offset: offset + rows * hidden].view(rows, hidden)
+
+        for _ in range(sets):
+            batch = {"x": row_view(torch.randn(rows * hidden + 8, device=device, dtype=torch.bfloat16,
+                                               generator=generator))}
+            if self.op != "rms_norm":
+                batch["r"] = row_view(torch.randn(rows * hidden + 8, device=device, dtype=torch.bfloat16,
+                                                  generator=generator))
+            if self.op == "rms_norm":
+                batch["out"] = torch.empty(rows, hidden, device=device, dtype=torch.bfloat16)
+            if self.op == "fused_add_rms_norm_static_fp8_quant":
+                batch["out"] = torch.empty(rows, hidden, device=device, dtype=torch.float8_e4m3fn)
+            batches.append(batch)
+        shared = {"w": (torch.randn(hidden, device=device, generator=generator) * 0.1 + 1.0).to(torch.bfloat16)}
+        if self.op == "fused_add_rms_norm_static_fp8_quant":
+            shared["scale"] = torch.tensor([0.05], dtype=torch.float32, device=device)
+        return batches, shared
+
+    def call(self, batch, shared) -> None:
+        import torch
+
+        ops = torch.ops.inference_performance_lab
+        eps = self.spec.get("eps")
+        if self.op == "silu_and_mul":
+            ops.silu_and_mul(batch["out"], batch["x"])
+        elif self.op == "rms_norm":
+            ops.rms_norm(batch["out"], batch["x"], shared["w"], eps)
+        elif self.op == "fused_add_rms_norm_static_fp8_quant":
+            ops.fused_add_rms_norm_static_fp8_quant(batch["out"], batch["x"], batch["r"], shared["w"],
+                                                    shared["scale"], eps)
+        else:
+            ops.fused_add_rms_norm(batch["x"], batch["r"], shared["w"], eps)
+
+    def plan(self, batch, shared, rows: int) -> str:
+        from inference_performance_lab.kernels import capi
+
+        if self.op == "silu_and_mul":
+            return capi.silu_and_mul_plan(batch["out"].data_ptr(), batch["x"].data_ptr(), rows,
+                                          self.spec["intermediate"])
+        hidden, w = self.spec["hidden"], shared["w"].data_ptr()
+        if self.op == "rms_norm":
+            return capi.rms_norm_plan(batch["out"].data_ptr(), batch["x"].data_ptr(), w, rows, hidden)
+        if self.op == "fused_add_rms_norm_static_fp8_quant":
+            return capi.fused_add_rms_norm_static_fp8_quant_plan(
+                batch["out"].data_ptr(), batch["x"].data_ptr(), batch["r"].data_ptr(), w, rows, hidden)
+        return capi.fused_add_rms_norm_plan(batch["x"].data_ptr(), batch["r"].data_ptr(), w, rows, hidden)
+
+    def e2e_inputs(self, batch):
+        """Device tensors an end-to-end step fills from pinned host memory."""
+        return [batch["x"]] if self.op in ("silu_and_mul", "rms_norm") else [batch["x"], batch["r"]]
+
+    def e2e_outputs(self, batch):
+        """Device tensors an end-to-end step reads back into pinned host memory."""
+        if self.op == "fused_add_rms_norm":
+            return [batch["x"], batch["r"]]
+        if self.op == "fused_add_rms_norm_static_fp8_quant":
+            return [batch["out"], batch["r"]]
+        return [batch["out"]]
+
+    def cpu_call(self, rows: int):
+        """The reference's CPU path (its torch fp32 oracle, restated in oracle/) on `rows` rows."""
+        import torch
+
+        from oracle import oracle
+
+        spec = self.spec
+        generator = torch.Generator().manual_seed(0)
+        if self.op == "silu_and_mul":
+            x = (torch.randn(rows, 2 * spec["intermediate"], generator=generator) * spec["std"]).to(torch.bfloat16)
+            return lambda: oracle.torch_silu_and_mul(x)
+        x = torch.randn(rows, spec["hidden"], generator=generator).to(torch.bfloat16)
+        r = torch.randn(rows, spec["hidden"], generator=generator).to(torch.bfloat16)
+        w = (torch.randn(spec["hidden"], generator=generator) * 0.1 + 1).to(torch.bfloat16)
+        eps = spec["eps"]
+        if self.op == "rms_norm":
+            return lambda: oracle.torch_rms_norm(x, w, eps)
+        if self.op == "fused_add_rms_norm_static_fp8_quant":
+            return lambda: oracle.torch_fused_add_rms_norm_static_fp8_quant(x, r, w, 0.05, eps)
+        return lambda: oracle.torch_fused_add_rms_norm(x, r, w, eps)
+
+    def metric(self) -> str:
+        return {
+            "silu_and_mul": "SiLU-and-mul achieved GB/s",
+            "rms_norm": "RMSNorm achieved HBM GB/s",
+            "fused_add_rms_norm_static_fp8_quant": "add+RMSNorm (fp8 out) achieved HBM GB/s",
+        }.get(self.op, "add+RMSNorm achieved HBM GB/s")
+
+    def traffic_elems(self, rows: int) -> tuple[int, int]:
+        """(bf16 elements read, bf16 elements written) of a torch op with the same DRAM bytes."""
+        if self.op == "silu_and_mul":
+            return 2 * rows * self.spec["intermediate"], rows * self.spec["intermediate"]
+        hidden = self.spec["hidden"]
+        if self.op == "rms_norm":
+            return rows * hidden, rows * hidden
+        if self.op == "fused_add_rms_norm_static_fp8_quant":
+            return 2 * rows * hidden, (3 * rows * hidden) // 2
+        return 2 * rows * hidden, 2 * rows * hidden
 
 
 # ------------------------------------------------------------------------------------------
@@ -252,20 +361,10 @@ def cpu_reference_rate(spec, seconds: float, sample_rows: int | None = None) -> 
     """Times the reference's CPU path on a bounded sample of the workload; GB/s of the metric."""
     import torch
 
-    from oracle import oracle
-
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     rows = spec["rows"] if sample_rows is None else sample_rows
-    generator = torch.Generator().manual_seed(0)
-    if spec["op"] == "silu_and_mul":
-        x = (torch.randn(rows, 2 * spec["intermediate"], generator=generator) * spec["std"]).to(torch.bfloat16)
-        call = lambda: oracle.torch_silu_and_mul(x)  # noqa: E731
-    else:
-        x = torch.randn(rows, spec["hidden"], generator=generator).to(torch.bfloat16)
-        r = torch.randn(rows, spec["hidden"], generator=generator).to(torch.bfloat16)
-        w = (torch.randn(spec["hidden"], generator=generator) * 0.1 + 1).to(torch.bfloat16)
-        call = lambda: oracle.torch_fused_add_rms_norm(x, r, w, spec["eps"])  # noqa: E731
+    call = OpWorkload(spec).cpu_call(rows)
     call()
     times = []
     start = time.perf_counter()
@@ -292,8 +391,6 @@ def run_reference(args, spec) -> None:
         return
     import torch
 
-    from oracle import oracle
-
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     # Size each step's sample so that warm-up + K steps end within about a minute.
@@ -301,15 +398,8 @@ def run_reference(args, spec) -> None:
     per_row = probe["ms_per_call"] / 1e3 / min(spec["rows"], 256)
     budget = 60.0 / max(args.steps + args.warmup, 1)
     rows = int(max(1, min(spec["rows"], budget / per_row)))
-    generator = torch.Generator().manual_seed(0)
-    if spec["op"] == "silu_and_mul":
-        x = (torch.randn(rows, 2 * spec["intermediate"], generator=generator) * spec["std"]).to(torch.bfloat16)
-        call = lambda: oracle.torch_silu_and_mul(x)  # noqa: E731
-    else:
-        x = torch.randn(rows, spec["hidden"], generator=generator).to(torch.bfloat16)
-        r = torch.randn(rows, spec["hidden"], generator=generator).to(torch.bfloat16)
-        w = (torch.randn(spec["hidden"], generator=generator) * 0.1 + 1).to(torch.bfloat16)
-        call = lambda: oracle.torch_fused_add_rms_norm(x, r, w, spec["eps"])  # noqa: E731
+    workload = OpWorkload(spec)
+    call = workload.cpu_call(rows)
     for _ in range(args.warmup):
         call()
     t0 = time.perf_counter()
@@ -320,7 +410,7 @@ def run_reference(args, spec) -> None:
     sample = f"{rows} of {spec['rows']} rows per step, torch fp32 on CPU ({threads} threads)"
     line = {
         "impl": "reference",
-        "metric": "add+RMSNorm achieved HBM GB/s" if spec["op"] != "silu_and_mul" else "SiLU-and-mul achieved GB/s",
+        "metric": workload.metric(),
         "value": value,
         "unit": "GB/s",
         "n_gpus": args.gpus,
@@ -328,7 +418,7 @@ def run_reference(args, spec) -> None:
         "warmup": args.warmup,
         "ms_per_step": elapsed / args.steps * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if spec.get("sharded") else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
@@ -347,7 +437,7 @@ def run_reference(args, spec) -> None:
 def run_ours(args, spec) -> None:
     import torch
 
-    from inference_performance_lab.kernels import extension
+    from inference_performance_lab.kernels import capi, extension
     from inference_performance_lab.kernels.sharding import row_shard, shard_seed
 
     if not torch.cuda.is_available():
@@ -358,32 +448,19 @@ def run_ours(args, spec) -> None:
     extension.load_extension()
     stream = torch.cuda.current_stream()
 
-    is_silu = spec["op"] == "silu_and_mul"
+    workload = OpWorkload(spec)
     if spec.get("sharded"):
-        shard = row_shard(spec["rows"], dist.world, dist.rank)
-        rows = shard.rows
+        rows = row_shard(spec["rows"], dist.world, dist.rank).rows
         scaling = "strong"
     else:
         rows = spec["rows"]
         scaling = "weak"
     per_step = step_bytes(spec, rows)
     sets = max(1, math.ceil(4 * L2_BYTES / per_step)) if per_step < 4 * L2_BYTES else 1
-    seed = shard_seed(0, dist.rank)
-    if is_silu:
-        batches = make_silu_sets(spec, seed, device, sets)
-        op = torch.ops.inference_performance_lab.silu_and_mul
+    batches, shared = workload.make_sets(rows, shard_seed(0, dist.rank), device, sets)
 
-        def step(i: int) -> None:
-            out, x = batches[i % sets]
-            op(out, x)
-    else:
-        batches, weight = make_rms_sets(spec, rows, seed, device, sets)
-        op = torch.ops.inference_performance_lab.fused_add_rms_norm
-        eps = spec["eps"]
-
-        def step(i: int) -> None:
-            x, r = batches[i % sets]
-            op(x, r, weight, eps)
+    def step(i: int) -> None:
+        workload.call(batches[i % sets], shared)
 
     with torch.inference_mode():
         for i in range(args.warmup):
@@ -427,13 +504,11 @@ def run_ours(args, spec) -> None:
         graph_ms_per_step = g0.elapsed_time(g1) / (replays * graph_steps)
         del graph
 
-        e2e = run_e2e(args, spec, rows, batches, weight if not is_silu else None, stream, dist)
-        same_traffic = copy_same_traffic(spec, rows, device, args.steps)
+        e2e = run_e2e(args, spec, workload, rows, batches[0], shared, stream, dist)
+        same_traffic = copy_same_traffic(workload, rows, device, args.steps)
 
     # Every bounded wait of the staged kernel must have completed: a nonzero fault word means a
     # kernel gave up and its outputs are incomplete, so the run is not a measurement.
-    from inference_performance_lab.kernels import capi
-
     fault_flags = int(dist.max(float(capi.device_fault_flags(dist.local_rank))))
     if fault_flags:
         raise SystemExit(f"device fault word {fault_flags:#x}: a kernel gave up on a wait")
@@ -453,7 +528,7 @@ def run_ours(args, spec) -> None:
         traffic = traffic * rows / WORKLOADS[args.workload]["rows"]
     total_rows = rows * dist.world if not spec.get("sharded") else spec["rows"]
     line = {
-        "metric": "add+RMSNorm achieved HBM GB/s" if not is_silu else "SiLU-and-mul achieved GB/s",
+        "metric": workload.metric(),
         "value": value,
         "unit": "GB/s",
         "n_gpus": dist.world,
@@ -471,7 +546,7 @@ def run_ours(args, spec) -> None:
             "bytes_per_step_per_rank": per_step,
             "l2": f"inputs rotate over {sets} batches ({sets * per_step / 1e6:.0f} MB per rank, "
                   f"> 4x the 126 MB L2)" if sets > 1 else "inputs larger than the 126 MB L2",
-            "kernel": kernel_plan(spec, batches, rows),
+            "kernel": workload.plan(batches[0], shared, rows),
         },
         "pct_of_peak": 100.0 * achieved / peak,
         "rows_per_s": total_rows / (ms_per_step * 1e-3),
@@ -499,27 +574,26 @@ def run_ours(args, spec) -> None:
     dist.close()
 
 
-def copy_same_traffic(spec, rows: int, device, steps: int) -> dict:
-    """A torch elementwise op moving the same DRAM bytes as one step (add+RMSNorm: copy of the
-    x+residual bytes; SiLU: add of the gate and up halves into the output), timed the same way
-    (back-to-back over rotating buffers > 4x L2, CUDA events): the practical bandwidth at this
-    transfer size, beside the large-copy peak."""
+def copy_same_traffic(workload, rows: int, device, steps: int) -> dict:
+    """A torch elementwise op moving the same DRAM bytes as one step (an add of two halves when the
+    step reads twice what it writes, as SiLU does, else a copy of half the step's bytes), timed
+    the same way (back-to-back over rotating buffers > 4x L2, CUDA events): the practical
+    bandwidth at this transfer size, beside the large-copy peak."""
     import torch
 
-    if spec["op"] == "silu_and_mul":
-        read_elems, write_elems = 2 * rows * spec["intermediate"], rows * spec["intermediate"]
-    else:
-        read_elems = write_elems = 2 * rows * spec["hidden"]
+    read_elems, write_elems = workload.traffic_elems(rows)
     per = 2 * (read_elems + write_elems)
+    use_add = read_elems == 2 * write_elems
+    n = write_elems if use_add else (read_elems + write_elems) // 2
     sets = max(1, math.ceil(4 * L2_BYTES / per)) if per < 4 * L2_BYTES else 1
-    src = [torch.empty(read_elems, dtype=torch.bfloat16, device=device).normal_() for _ in range(sets)]
-    dst = [torch.empty(write_elems, dtype=torch.bfloat16, device=device) for _ in range(sets)]
-    if read_elems == write_elems:
+    src = [torch.empty(2 * n if use_add else n, dtype=torch.bfloat16, device=device).normal_() for _ in range(sets)]
+    dst = [torch.empty(n, dtype=torch.bfloat16, device=device) for _ in range(sets)]
+    if use_add:
+        def one(i: int) -> None:
+            torch.add(src[i % sets][:n], src[i % sets][n:], out=dst[i % sets])
+    else:
         def one(i: int) -> None:
             dst[i % sets].copy_(src[i % sets])
-    else:
-        def one(i: int) -> None:
-            torch.add(src[i % sets][:write_elems], src[i % sets][write_elems:], out=dst[i % sets])
     steps = max(3, min(steps, int(20e9 // per)))
     for i in range(3):
         one(i)
@@ -531,54 +605,31 @@ def copy_same_traffic(spec, rows: int, device, steps: int) -> dict:
     e1.record()
     e1.synchronize()
     us = e0.elapsed_time(e1) / steps * 1e3
-    return {"op": "torch copy" if read_elems == write_elems else "torch add", "us_per_launch": us,
+    return {"op": "torch add" if use_add else "torch copy", "us_per_launch": us,
             "achieved": per / (us * 1e-6) / 1e9}
 
 
-def kernel_plan(spec, batches, rows: int) -> str:
-    from inference_performance_lab.kernels import capi
-
-    if spec["op"] == "silu_and_mul":
-        out, x = batches[0]
-        return capi.silu_and_mul_plan(out.data_ptr(), x.data_ptr(), rows, spec["intermediate"])
-    x, r = batches[0]
-    return capi.fused_add_rms_norm_plan(x.data_ptr(), r.data_ptr(), x.data_ptr(), rows, spec["hidden"])
-
-
-def run_e2e(args, spec, rows: int, batches, weight, stream, dist) -> dict:
+def run_e2e(args, spec, workload, rows: int, batch, shared, stream, dist) -> dict:
     """The metric through the public op, with each step's inputs copied from pinned host memory
     and its results copied back inside the timed region."""
     import torch
 
-    from inference_performance_lab.kernels import extension
-
     per_step = step_bytes(spec, rows)
     # Bounded: a step moves 2x its bytes over PCIe; keep the region to a few seconds.
     steps = max(3, min(args.steps, args.e2e_steps, int(20e9 // per_step)))
-    if spec["op"] == "silu_and_mul":
-        out_d, x_d = batches[0]
-        x_h = x_d.cpu().pin_memory()
-        out_h = torch.empty(out_d.shape, dtype=out_d.dtype, pin_memory=True)
-        h2d, d2h = x_h.numel() * 2, out_h.numel() * 2
+    inputs = workload.e2e_inputs(batch)
+    outputs = workload.e2e_outputs(batch)
+    inputs_h = [t.cpu().pin_memory() for t in inputs]
+    outputs_h = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outputs]
+    h2d = sum(t.numel() * t.element_size() for t in inputs_h)
+    d2h = sum(t.numel() * t.element_size() for t in outputs_h)
 
-        def one() -> None:
-            x_d.copy_(x_h, non_blocking=True)
-            torch.ops.inference_performance_lab.silu_and_mul(out_d, x_d)
-            out_h.copy_(out_d, non_blocking=True)
-    else:
-        x_d, r_d = batches[0]
-        x_h, r_h = x_d.cpu().pin_memory(), r_d.cpu().pin_memory()
-        xo_h = torch.empty_like(x_h).pin_memory()
-        ro_h = torch.empty_like(r_h).pin_memory()
-        h2d = d2h = 2 * x_h.numel() * 2
-        eps = spec["eps"]
-
-        def one() -> None:
-            x_d.copy_(x_h, non_blocking=True)
-            r_d.copy_(r_h, non_blocking=True)
-            extension.fused_add_rms_norm(x_d, r_d, weight, eps)
-            xo_h.copy_(x_d, non_blocking=True)
-            ro_h.copy_(r_d, non_blocking=True)
+    def one() -> None:
+        for d, h in zip(inputs, inputs_h):
+            d.copy_(h, non_blocking=True)
+        workload.call(batch, shared)
+        for d, h in zip(outputs, outputs_h):
+            h.copy_(d, non_blocking=True)
 
     for _ in range(min(3, steps)):
         one()
