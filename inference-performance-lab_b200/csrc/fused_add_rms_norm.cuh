@@ -26,6 +26,13 @@
 // * rmsnorm_warp_kernel - short rows (H <= 1024, H % 8 == 0, 16-byte aligned): a warp per row,
 //   values in registers, vector loads; see below.
 //
+// * rmsnorm_cta_kernel - few rows (decode batches, up to 256) of 16-byte aligned rows with
+//   1024 < H <= 16384: a CTA per row, the row in registers, one memory round trip.
+//
+// * rmsnorm_stash_kernel - many 16-byte aligned rows beyond what the staged kernel holds at once
+//   (and H <= 1536): a small CTA for every row, the fp32 sum parked in shared memory between the
+//   passes. The planner (ipl_b200.cu) gives the measured crossovers.
+//
 // * rmsnorm_rowwise_kernel - the general fallback for any alignment (e.g. only one of x and
 //   residual misaligned, as in the reference's misaligned tests) and for rows too long to
 //   stage: one CTA per row, coalesced 2-byte accesses, values cached in registers when
@@ -265,7 +272,7 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
             bulk_load(smem_base + layout.weight_raw_offset, reinterpret_cast<const void*>(wbase), wbytes,
                       weight_bar, l2_policy_evict_last());
 
-            const uint64_t policy = l2_policy_evict_first();
+            const uint64_t policy = l2_policy_evict_first();  // normal and evict_last measured no faster
             for (int j = 0; j < local_rows; ++j) {
                 const int s = j % p.stages;
                 const int round = j / p.stages;
@@ -548,6 +555,226 @@ __global__ void __launch_bounds__(kWarpRowThreads) rmsnorm_warp_kernel(const War
                     store_fp8_chunk(p.out8 + row * p.hidden + 8 * c, v[i], true, 8 * c, p.hidden);
                 } else {
                     st_v4(orow + 8 * c, chunk_to_bf16(v[i]));
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Few rows of any width up to 16384 (decode-sized batches; H % 8 == 0, 16-byte aligned rows): one
+// CTA per row, every value in registers. Each thread owns kChunks 16-byte chunks of the row and
+// issues the loads of its gamma, x and residual chunks back to back, so a row costs one memory
+// round trip, one warp-shuffle reduction and one __syncthreads. The staged kernel's bulk copies,
+// mbarrier hand-off and shared-memory gamma pay off when a CTA streams many rows; for a handful of
+// rows they are latency on the critical path.
+
+constexpr int kCtaRowMaxThreads = 512;
+
+// Gamma chunk c (8 bf16) as four packed pairs: one 16-byte load (kept in L1, since every CTA on
+// the SM reads the same gamma) when gamma is 16-byte aligned, eight 2-byte loads otherwise.
+__device__ __forceinline__ U32x4 load_weight_chunk(const uint16_t* weight, int c, bool aligned) {
+    if (aligned) return ld_shared_ro_v4(weight + 8 * c);
+    U32x4 w;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        w.v[e] = static_cast<uint32_t>(weight[8 * c + 2 * e]) | (static_cast<uint32_t>(weight[8 * c + 2 * e + 1]) << 16);
+    }
+    return w;
+}
+constexpr int kCtaRowMaxHidden = 4 * 8 * kCtaRowMaxThreads;  // 16384: four chunks per thread
+#ifdef IPL_TUNING_CTA_ROWS
+constexpr int64_t kCtaRowMaxRows = IPL_TUNING_CTA_ROWS;
+#else
+constexpr int64_t kCtaRowMaxRows = 256;
+#endif
+
+template <int kChunks, int kMode>
+__global__ void __launch_bounds__(kCtaRowMaxThreads) rmsnorm_cta_kernel(const WarpRowParams p) {
+    constexpr bool kResidual = kMode != kModePlain;
+    constexpr bool kFp8 = kMode == kModeFusedFp8;
+    __shared__ float partials[2][kCtaRowMaxThreads / kWarpSize];
+    const int chunks = p.hidden >> 3;
+    const int warps = static_cast<int>(blockDim.x) / kWarpSize;
+    const int warp = threadIdx.x / kWarpSize;
+    const int lane = threadIdx.x % kWarpSize;
+    const float hidden_f = static_cast<float>(p.hidden);
+
+    // Every input (gamma and the scale included) may have been written by the previous kernel.
+    grid_dependency_wait();
+    grid_launch_dependents();
+    U32x4 wraw[kChunks];
+    const bool weight_aligned = (reinterpret_cast<uintptr_t>(p.weight) & 15u) == 0;
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+        const int c = threadIdx.x + static_cast<int>(blockDim.x) * i;
+        if (c < chunks) wraw[i] = load_weight_chunk(p.weight, c, weight_aligned);
+    }
+    const float scale_inv = kFp8 ? 1.0f / *p.scale : 1.0f;
+    const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
+
+    int parity = 0;
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const uint16_t* xr = p.x + row * p.hidden;
+        uint16_t* rr = kResidual ? p.residual + row * p.hidden : nullptr;
+        U32x4 xs[kChunks], rs[kChunks];
+#pragma unroll
+        for (int i = 0; i < kChunks; ++i) {
+            const int c = threadIdx.x + static_cast<int>(blockDim.x) * i;
+            if (c < chunks) {
+                xs[i] = ld_v4(xr + 8 * c);
+                if constexpr (kResidual) rs[i] = ld_v4(rr + 8 * c);
+            }
+        }
+        Pairs4 v[kChunks];
+        F32x2 acc = f32x2_make(0.0f, 0.0f);
+#pragma unroll
+        for (int i = 0; i < kChunks; ++i) {
+            const int c = threadIdx.x + static_cast<int>(blockDim.x) * i;
+            if (c < chunks) {
+                if constexpr (kResidual) {
+                    v[i] = chunk_sum(xs[i], rs[i]);
+                    st_v4(rr + 8 * c, chunk_to_bf16(v[i]));
+                } else {
+                    v[i] = chunk_widen(xs[i]);
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc = f32x2_fma(v[i].v[e], v[i].v[e], acc);
+            }
+        }
+        float acc_lo, acc_hi;
+        f32x2_split(acc, acc_lo, acc_hi);
+        const float warp_total = warp_sum(acc_lo + acc_hi);
+        // Two parities of partials: row k + 1 writes the other set, and row k + 2 can only write
+        // this one after every thread has passed row k + 1's barrier, i.e. finished reading it.
+        if (lane == 0) partials[parity][warp] = warp_total;
+        __syncthreads();
+        float sumsq = 0.0f;
+        for (int w = 0; w < warps; ++w) sumsq += partials[parity][w];
+        parity ^= 1;
+        const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
+        const F32x2 inv2 = f32x2_make(inv, inv);
+#pragma unroll
+        for (int i = 0; i < kChunks; ++i) {
+            const int c = threadIdx.x + static_cast<int>(blockDim.x) * i;
+            if (c < chunks) {
+                const Pairs4 w = chunk_widen(wraw[i]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) v[i].v[e] = f32x2_mul(f32x2_mul(v[i].v[e], inv2), w.v[e]);
+                if constexpr (kFp8) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) v[i].v[e] = f32x2_mul(v[i].v[e], scale_inv2);
+                    store_fp8_chunk(p.out8 + row * p.hidden + 8 * c, v[i], true, 8 * c, p.hidden);
+                } else {
+                    st_v4(p.out + row * p.hidden + 8 * c, chunk_to_bf16(v[i]));
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Many rows of moderate width (H % 8 == 0, 16-byte aligned rows, 1024 < H <= 16384): a small CTA
+// for every row - H / 32 threads (a multiple of 32, 64..512), each owning up to four 16-byte
+// chunks whose loads it issues back to back - so a row costs one memory round trip per pass and
+// the hardware keeps many rows per SM in flight, starting the next as soon as one retires. Pass 1
+// reads x and residual, writes residual and parks the fp32 sum v in shared memory (4H bytes);
+// pass 2 reads v back, so HBM sees each byte once and registers do not hold the row across the
+// reduction.
+
+constexpr int kStashChunks = 4;  // 16-byte chunks per thread: all of a thread's loads in flight at once
+constexpr int kStashMinThreads = 64;
+constexpr int kStashMaxThreads = 512;
+constexpr int kStashMaxHidden = 12288;  // the planner's limit; the kernel itself takes up to 16384
+constexpr int64_t kStagedStreamingElements = int64_t{1} << 28;  // from here on the staged ring streams faster
+
+__host__ __device__ constexpr uint32_t stash_smem_bytes(int hidden) { return static_cast<uint32_t>(hidden) * 4u; }
+
+template <int kUnroll, int kMode>
+__global__ void __launch_bounds__(kStashMaxThreads) rmsnorm_stash_kernel(const WarpRowParams p) {
+    constexpr bool kResidual = kMode != kModePlain;
+    constexpr bool kFp8 = kMode == kModeFusedFp8;
+    extern __shared__ __align__(128) unsigned char smem[];  // v: chunk k as 32 bytes at 32k
+    __shared__ float partials[2][kStashMaxThreads / kWarpSize];
+    const uint32_t vbase = smem_addr(smem);
+    const int threads = static_cast<int>(blockDim.x);
+    const int step = threads * kUnroll;
+    const int warps = threads / kWarpSize;
+    const int chunks = p.hidden >> 3;
+    const int warp = threadIdx.x / kWarpSize;
+    const int lane = threadIdx.x % kWarpSize;
+    const float hidden_f = static_cast<float>(p.hidden);
+    const bool weight_aligned = (reinterpret_cast<uintptr_t>(p.weight) & 15u) == 0;
+
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const float scale_inv = kFp8 ? 1.0f / *p.scale : 1.0f;
+    const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
+
+    int parity = 0;
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const uint16_t* xr = p.x + row * p.hidden;
+        uint16_t* rr = kResidual ? p.residual + row * p.hidden : nullptr;
+        F32x2 acc = f32x2_make(0.0f, 0.0f);
+        for (int c0 = threadIdx.x; c0 < chunks; c0 += step) {
+            U32x4 xs[kUnroll], rs[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int c = c0 + u * threads;
+                if (c < chunks) {
+                    xs[u] = ld_v4(xr + 8 * c);
+                    if constexpr (kResidual) rs[u] = ld_v4(rr + 8 * c);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int c = c0 + u * threads;
+                if (c < chunks) {
+                    Pairs4 v;
+                    if constexpr (kResidual) {
+                        v = chunk_sum(xs[u], rs[u]);
+                        st_v4(rr + 8 * c, chunk_to_bf16(v));
+                    } else {
+                        v = chunk_widen(xs[u]);
+                    }
+                    sts_pairs(vbase + 32u * c, v.v[0], v.v[1]);
+                    sts_pairs(vbase + 32u * c + 16u, v.v[2], v.v[3]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc = f32x2_fma(v.v[e], v.v[e], acc);
+                }
+            }
+        }
+        float acc_lo, acc_hi;
+        f32x2_split(acc, acc_lo, acc_hi);
+        const float warp_total = warp_sum(acc_lo + acc_hi);
+        if (lane == 0) partials[parity][warp] = warp_total;  // two parities: see rmsnorm_cta_kernel
+        __syncthreads();
+        float sumsq = 0.0f;
+        for (int w = 0; w < warps; ++w) sumsq += partials[parity][w];
+        parity ^= 1;
+        const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
+        const F32x2 inv2 = f32x2_make(inv, inv);
+
+        // Each thread reads back only the chunks it wrote, so the next row's pass 1 cannot
+        // overwrite v that another thread still needs.
+        for (int c0 = threadIdx.x; c0 < chunks; c0 += step) {
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int c = c0 + u * threads;
+                if (c < chunks) {
+                    Pairs4 v;
+                    lds_pairs(vbase + 32u * c, v.v[0], v.v[1]);
+                    lds_pairs(vbase + 32u * c + 16u, v.v[2], v.v[3]);
+                    const Pairs4 w = chunk_widen(load_weight_chunk(p.weight, c, weight_aligned));
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) v.v[e] = f32x2_mul(f32x2_mul(v.v[e], inv2), w.v[e]);
+                    if constexpr (kFp8) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) v.v[e] = f32x2_mul(v.v[e], scale_inv2);
+                        store_fp8_chunk(p.out8 + row * p.hidden + 8 * c, v, true, 8 * c, p.hidden);
+                    } else {
+                        st_v4(p.out + row * p.hidden + 8 * c, chunk_to_bf16(v));
+                    }
                 }
             }
         }

@@ -30,7 +30,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
     std::atomic<int> sm_count{0};
     std::atomic<int> max_smem_optin{0};
-    std::atomic<uint32_t> smem_configured{0};  // bit per staged-kernel instance
+    std::atomic<uint32_t> smem_configured{0};  // bit per kernel instance given the shared-memory opt-in
 };
 DeviceInfo g_devices[kMaxDevices];
 
@@ -81,12 +81,13 @@ cudaError_t launch(Kernel kernel, unsigned grid, unsigned block, size_t smem, cu
 // ------------------------------------------------------------------------------------------
 // add + RMSNorm / RMSNorm planning
 
-enum class RmsFamily { kNone, kStaged, kWarpRow, kRowwiseCached, kRowwiseTwoPass };
+enum class RmsFamily { kNone, kStaged, kWarpRow, kCtaRow, kStash, kRowwiseCached, kRowwiseTwoPass };
 
 struct RmsPlan {
     RmsFamily family = RmsFamily::kNone;
     int warps_per_row = 0;  // staged kernels: 1, 2, 4, 8 or 16
-    int chunks_per_lane = 0;  // warp-per-row kernel: 1, 2, 4 or 8
+    int chunks_per_lane = 0;  // warp- and CTA-per-row kernels: 16-byte chunks per thread (1, 2 or 4)
+    unsigned threads = 0;     // CTA-per-row kernel: block size
     unsigned grid = 0;
     size_t smem = 0;
     StagedParams staged = {};
@@ -105,6 +106,12 @@ const char* rms_kernel_name(const RmsPlan& plan, int mode) {
         {"rmsnorm_warp_kernel<1>", "rmsnorm_warp_kernel<2>", "rmsnorm_warp_kernel<4>"},
         {"rmsnorm_warp_kernel<1, plain>", "rmsnorm_warp_kernel<2, plain>", "rmsnorm_warp_kernel<4, plain>"},
         {"rmsnorm_warp_kernel<1, fp8>", "rmsnorm_warp_kernel<2, fp8>", "rmsnorm_warp_kernel<4, fp8>"}};
+    static const char* const kCtaNames[3][3] = {
+        {"rmsnorm_cta_kernel<1>", "rmsnorm_cta_kernel<2>", "rmsnorm_cta_kernel<4>"},
+        {"rmsnorm_cta_kernel<1, plain>", "rmsnorm_cta_kernel<2, plain>", "rmsnorm_cta_kernel<4, plain>"},
+        {"rmsnorm_cta_kernel<1, fp8>", "rmsnorm_cta_kernel<2, fp8>", "rmsnorm_cta_kernel<4, fp8>"}};
+    static const char* const kStashNames[3] = {"rmsnorm_stash_kernel<4>", "rmsnorm_stash_kernel<4, plain>",
+                                               "rmsnorm_stash_kernel<4, fp8>"};
     static const char* const kRowwiseNames[3][2] = {
         {"rmsnorm_rowwise_kernel<cached>", "rmsnorm_rowwise_kernel<two-pass>"},
         {"rmsnorm_rowwise_kernel<cached, plain>", "rmsnorm_rowwise_kernel<two-pass, plain>"},
@@ -118,6 +125,10 @@ const char* rms_kernel_name(const RmsPlan& plan, int mode) {
         case RmsFamily::kWarpRow:
             while ((1 << i) < plan.chunks_per_lane) ++i;
             return kWarpNames[mode][i];
+        case RmsFamily::kCtaRow:
+            while ((1 << i) < plan.chunks_per_lane) ++i;
+            return kCtaNames[mode][i];
+        case RmsFamily::kStash: return kStashNames[mode];
         case RmsFamily::kRowwiseCached: return kRowwiseNames[mode][0];
         case RmsFamily::kRowwiseTwoPass: return kRowwiseNames[mode][1];
     }
@@ -178,6 +189,57 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         plan.smem = static_cast<size_t>(hidden) * 4u;
         return plan;
     }
+    // Aligned rows of 1024 < H <= 16384 have three kernels. The choice, from cold-L2 sweeps on
+    // B200 against each other and vLLM's kernel (257..8192 rows, H 1536..16384):
+    // * up to 256 rows (decode batches): a CTA per row with the row in registers - one memory
+    //   round trip, no shared-memory hand-off; 25-35 % under the others' latency;
+    // * a grid of CTAs whose rows all fit in shared memory at once (at most max_stages rows per
+    //   SM): the staged kernel, which requests every row at the start;
+    // * more rows than that, or H <= 1536: a small CTA for every row (stash kernel), which
+    //   streams like a copy and beat the staged ring by 2-11 % there;
+    // * launches of 2^28 elements or more (2 GB of traffic, e.g. 32768 x 8192): the staged ring
+    //   again, whose per-row cost is the lower one once its start-up and drain are amortised
+    //   (97.9 % against 94.7 % of the copy peak at 262144 x 8192);
+    // * H > 12288: the staged kernel at any row count (the stash kernel's 512-thread CTAs lost
+    //   20-30 %).
+    const bool vector_rows = hidden % 8 == 0 && hidden <= kCtaRowMaxHidden && ((xa | oa) & 15u) == 0 && fp8_vector_ok;
+    const int64_t resident_rows = static_cast<int64_t>(sm_count) * max_stages;
+    const bool same_phase = (xa & 15u) == (oa & 15u);
+#if defined(IPL_TUNING_FAMILY)
+    const int family_choice = IPL_TUNING_FAMILY;  // 1 CTA per row, 2 stash, 3 staged
+#else
+    const int family_choice = rows <= kCtaRowMaxRows                           ? 1
+                              : hidden > kStashMaxHidden                         ? 3
+                              : rows * hidden >= kStagedStreamingElements        ? 3
+                              : hidden <= 1536                                   ? 2
+                              : rows <= resident_rows && same_phase              ? 3
+                                                                                 : 2;
+#endif
+    // Many aligned rows of moderate width: a small CTA for every row, v parked in shared memory.
+    if (vector_rows && family_choice == 2) {
+        // Up to kStashChunks chunks a thread (H <= 16384 needs at most 512 threads).
+        const int64_t row_chunks = hidden / 8;
+        const int64_t per_warp = static_cast<int64_t>(kStashChunks) * kWarpSize;
+        int64_t threads = (row_chunks + per_warp - 1) / per_warp * kWarpSize;
+        threads = threads < kStashMinThreads ? kStashMinThreads : threads;
+        plan.family = RmsFamily::kStash;
+        plan.chunks_per_lane = kStashChunks;
+        plan.threads = static_cast<unsigned>(threads);
+        plan.smem = stash_smem_bytes(static_cast<int>(hidden));
+        plan.grid = static_cast<unsigned>(rows < INT_MAX ? rows : INT_MAX);
+        return plan;
+    }
+    // Few aligned rows: a CTA per row, values in registers.
+    if (vector_rows && family_choice == 1) {
+        const int64_t row_chunks = hidden / 8;
+        const int64_t per_thread = (row_chunks + kCtaRowMaxThreads - 1) / kCtaRowMaxThreads;
+        plan.family = RmsFamily::kCtaRow;
+        plan.chunks_per_lane = per_thread <= 1 ? 1 : per_thread <= 2 ? 2 : 4;
+        const int64_t threads = (row_chunks + plan.chunks_per_lane - 1) / plan.chunks_per_lane;
+        plan.threads = static_cast<unsigned>((threads + kWarpSize - 1) / kWarpSize * kWarpSize);
+        plan.grid = static_cast<unsigned>(rows < INT_MAX ? rows : INT_MAX);  // a CTA for every row
+        return plan;
+    }
     if ((xa & 15u) == (oa & 15u) && max_stages >= 2 && fp8_vector_ok) {
         const int grid = static_cast<int>(rows < sm_count ? rows : sm_count);
         const int64_t rows_per_cta = (rows + grid - 1) / grid;
@@ -230,6 +292,27 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
 
 const char* mode_label(int mode) {
     return mode == kModeFused ? "fused RMSNorm" : mode == kModePlain ? "RMSNorm" : "fused RMSNorm fp8";
+}
+
+// Dynamic plus static shared memory above 48 KB (from H = 12288 on) needs the opt-in attribute; it
+// is set at the first launch per device and kernel instance, whatever the size.
+template <int kMode>
+ipl_status launch_stash(const RmsPlan& plan, DeviceInfo* info, cudaStream_t stream, const WarpRowParams& w) {
+    auto kernel = rmsnorm_stash_kernel<kStashChunks, kMode>;
+    const int bit = 21 + kMode;  // bits 21..23; the staged kernels use 0..20
+    if (!(info->smem_configured.load(std::memory_order_acquire) & (1u << bit))) {
+        const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     static_cast<int>(stash_smem_bytes(kCtaRowMaxHidden)));
+        if (err != cudaSuccess) {
+            return fail(IPL_ERROR_CUDA, "%s kernel setup failed: %s", mode_label(kMode), cudaGetErrorString(err));
+        }
+        info->smem_configured.fetch_or(1u << bit, std::memory_order_acq_rel);
+    }
+    const cudaError_t err = launch(kernel, plan.grid, plan.threads, plan.smem, stream, w);
+    if (err != cudaSuccess) {
+        return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
+    }
+    return IPL_SUCCESS;
 }
 
 template <int W, int kMode>
@@ -301,6 +384,41 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8
                 return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
             }
             return IPL_SUCCESS;
+        }
+        case RmsFamily::kCtaRow: {
+            WarpRowParams w;
+            w.x = x;
+            w.residual = residual;
+            w.out = out;
+            w.out8 = out8;
+            w.scale = scale;
+            w.weight = weight;
+            w.rows = rows;
+            w.hidden = static_cast<int>(hidden);
+            w.epsilon = plan.staged.epsilon;
+            cudaError_t err = cudaSuccess;
+            switch (plan.chunks_per_lane) {
+                case 1: err = launch(rmsnorm_cta_kernel<1, kMode>, plan.grid, plan.threads, 0, stream, w); break;
+                case 2: err = launch(rmsnorm_cta_kernel<2, kMode>, plan.grid, plan.threads, 0, stream, w); break;
+                default: err = launch(rmsnorm_cta_kernel<4, kMode>, plan.grid, plan.threads, 0, stream, w); break;
+            }
+            if (err != cudaSuccess) {
+                return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
+            }
+            return IPL_SUCCESS;
+        }
+        case RmsFamily::kStash: {
+            WarpRowParams w;
+            w.x = x;
+            w.residual = residual;
+            w.out = out;
+            w.out8 = out8;
+            w.scale = scale;
+            w.weight = weight;
+            w.rows = rows;
+            w.hidden = static_cast<int>(hidden);
+            w.epsilon = plan.staged.epsilon;
+            return launch_stash<kMode>(plan, info, stream, w);
         }
         case RmsFamily::kRowwiseCached:
         case RmsFamily::kRowwiseTwoPass: {

@@ -136,6 +136,14 @@ __device__ __forceinline__ U32x4 ld_v4(const void* p) {
                  : "l"(p));
     return r;
 }
+// Read-only 16-byte load that may stay in L1 (data every CTA on the SM reads, e.g. gamma).
+__device__ __forceinline__ U32x4 ld_shared_ro_v4(const void* p) {
+    U32x4 r;
+    asm volatile("ld.global.nc.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3])
+                 : "l"(p));
+    return r;
+}
 __device__ __forceinline__ void st_v2(void* p, uint32_t a, uint32_t b) {
     asm volatile("st.global.v2.b32 [%0], {%1,%2};" ::"l"(p), "r"(a), "r"(b) : "memory");
 }

@@ -85,7 +85,8 @@ def test_plain_rms_in_place_is_accepted_by_the_plan() -> None:
     # output == input is allowed (vLLM calls it out of place, callers may reuse the buffer).
     assert capi.rms_norm_plan(BASE, BASE, BASE + 8192, 2048, 3584) == "rmsnorm_staged_kernel<2, plain>"
     assert capi.rms_norm_plan(BASE + 2, BASE, BASE + 8192, 8, 3584) == "rmsnorm_rowwise_kernel<cached, plain>"
-    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 1, 8192) == "rmsnorm_staged_kernel<16, plain>"
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 1, 8192) == "rmsnorm_cta_kernel<2, plain>"
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 8192, 8192) == "rmsnorm_stash_kernel<4, plain>"
 
 
 def test_fp8_quant_arguments_and_plans() -> None:
@@ -96,6 +97,8 @@ def test_fp8_quant_arguments_and_plans() -> None:
     plan = capi.fused_add_rms_norm_static_fp8_quant_plan
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 3584) == "rmsnorm_staged_kernel<2, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 1024) == "rmsnorm_warp_kernel<4, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 7, 3584) == "rmsnorm_cta_kernel<1, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 9000, 4096) == "rmsnorm_stash_kernel<4, fp8>"
     # fp8 vector stores need 16-byte aligned rows and an 8-byte aligned output.
     assert plan(BASE + 4, BASE + 4098, BASE + (1 << 34) + 2, BASE + 12288, 2048, 3584).startswith(
         "rmsnorm_rowwise_kernel"
@@ -152,26 +155,43 @@ def test_rms_plan_selection() -> None:
     # Only one of them misaligned (the reference's misaligned tests): the general row kernel.
     assert rms_plan(1, 0, 0, 8, 3584) == "rmsnorm_rowwise_kernel<cached>"
     assert rms_plan(0, 1, 0, 8, 3584) == "rmsnorm_rowwise_kernel<cached>"
-    # A misaligned weight does not matter: gamma is staged in shared memory.
-    assert rms_plan(0, 0, 1, 8, 3584).startswith("rmsnorm_staged_kernel")
-    # Few rows: more warps share a row.
-    assert rms_plan(0, 0, 0, 1, 3584) == "rmsnorm_staged_kernel<16>"
+    # Up to 256 aligned rows (decode batches): a CTA per row, the row in registers; a misaligned
+    # weight is loaded element by element.
+    assert rms_plan(0, 0, 1, 8, 3584) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 0, 1, 3584) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 0, 256, 8192) == "rmsnorm_cta_kernel<2>"
+    assert rms_plan(0, 0, 0, 5, 16384) == "rmsnorm_cta_kernel<4>"
+    assert rms_plan(0, 0, 0, 5, 2048) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 0, 64, 2056) == "rmsnorm_cta_kernel<1>"
+    # More rows, all of them in shared memory at once (up to 14 per SM at H = 3584): the staged
+    # kernel, more warps per row when a CTA has fewer rows.
     assert rms_plan(0, 0, 0, 148 * 2, 3584) == "rmsnorm_staged_kernel<8>"
     assert rms_plan(0, 0, 0, 148 * 4, 3584) == "rmsnorm_staged_kernel<4>"
-    # Streaming (more rows than fit): about 128 KB in flight, one stage per group.
-    assert rms_plan(0, 0, 0, 148 * 16, 3584) == "rmsnorm_staged_kernel<2>"
+    assert rms_plan(0, 0, 0, 148 * 14, 3584) == "rmsnorm_staged_kernel<2>"
+    # Beyond that: a small CTA for every row (128 threads of four chunks at H = 3584).
+    assert rms_plan(0, 0, 0, 148 * 14 + 1, 3584) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 148 * 16, 3584) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 32768, 3584) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 16384, 8192) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 1000, 1536) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 20000, 12288) == "rmsnorm_stash_kernel<4>"
+    # From 2^28 elements a launch (the row-sharded workload's shard at 1..8 GPUs) streams through
+    # the staged ring: about 128 KB in flight, one stage per group (four 32 KB rows at H = 8192).
+    assert rms_plan(0, 0, 0, 262144, 8192) == "rmsnorm_staged_kernel<4>"
+    assert rms_plan(0, 0, 0, 32768, 8192) == "rmsnorm_staged_kernel<4>"
+    assert rms_plan(0, 0, 0, 100000, 12288) == "rmsnorm_staged_kernel<8>"
+    # Rows longer than 12288: the staged kernel, streaming two 64 KB stages.
+    assert rms_plan(0, 0, 0, 32768, 16384) == "rmsnorm_staged_kernel<8>"
     # Short aligned rows: a warp per row.
     assert rms_plan(0, 0, 0, 148 * 64, 1024) == "rmsnorm_warp_kernel<4>"
     assert rms_plan(0, 0, 3, 5, 1000) == "rmsnorm_warp_kernel<4>"
-    assert rms_plan(0, 0, 0, 5, 2048).startswith("rmsnorm_staged_kernel")
     assert rms_plan(0, 0, 0, 5, 256) == "rmsnorm_warp_kernel<1>"
     assert rms_plan(1, 1, 0, 5, 1024).startswith("rmsnorm_staged_kernel")
-    # The row-sharded workload's hidden size: four 32 KB rows in flight, 4 warps each.
-    assert rms_plan(0, 0, 0, 262144, 8192) == "rmsnorm_staged_kernel<4>"
-    assert rms_plan(0, 0, 0, 32768, 8192) == "rmsnorm_staged_kernel<4>"
-    # Odd widths stay on the staged kernel when x and residual share their offset.
+    # Widths that are not a multiple of 8 stay on the staged kernel when x and residual share
+    # their offset.
     assert rms_plan(0, 0, 0, 64, 1001).startswith("rmsnorm_staged_kernel")
-    assert rms_plan(0, 0, 0, 64, 2056).startswith("rmsnorm_staged_kernel")
+    assert rms_plan(0, 0, 0, 64, 2052).startswith("rmsnorm_staged_kernel")
+    assert rms_plan(0, 0, 0, 100000, 3580).startswith("rmsnorm_staged_kernel")
     # Rows too long for two stages fall back to the two-pass row kernel.
     assert rms_plan(0, 0, 0, 64, 40000) == "rmsnorm_rowwise_kernel<two-pass>"
     assert rms_plan(1, 0, 0, 64, 40000) == "rmsnorm_rowwise_kernel<two-pass>"
