@@ -201,7 +201,10 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
     //   again, whose per-row cost is the lower one once its start-up and drain are amortised
     //   (97.9 % against 94.7 % of the copy peak at 262144 x 8192);
     // * H > 12288: the staged kernel at any row count (the stash kernel's 512-thread CTAs lost
-    //   20-30 %).
+    //   20-30 %);
+    // * plain RMSNorm with H > 2048: the staged kernel at any row count. With only x to read a
+    //   stash thread keeps half the bytes in flight, and the staged ring was 5-28 % faster
+    //   (80.8 against 103.4 us at 32768 x 3584).
     const bool vector_rows = hidden % 8 == 0 && hidden <= kCtaRowMaxHidden && ((xa | oa) & 15u) == 0 && fp8_vector_ok;
     const int64_t resident_rows = static_cast<int64_t>(sm_count) * max_stages;
     const bool same_phase = (xa & 15u) == (oa & 15u);
@@ -211,6 +214,7 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
     const int family_choice = rows <= kCtaRowMaxRows                           ? 1
                               : hidden > kStashMaxHidden                         ? 3
                               : rows * hidden >= kStagedStreamingElements        ? 3
+                              : !residual && hidden > 2048 && same_phase         ? 3
                               : hidden <= 1536                                   ? 2
                               : rows <= resident_rows && same_phase              ? 3
                                                                                  : 2;
@@ -250,7 +254,8 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         //   having every row requested at the start shortens both;
         // * a CTA that streams more rows than fit keeps about 128 KB in flight with one stage per
         //   group (S = G): 4 x 32 KB rows at H = 8192 ran at 97 % of the copy peak, deeper rings
-        //   at 91 %.
+        //   at 91 %. The fp8 output's conversion makes pass 2 heavier: there half the groups, each
+        //   of twice the warps, share the same ring (S = 2G), 3-7 % faster at 32768 rows.
         int stages;
         int groups;
         if (rows_per_cta <= max_stages) {
@@ -263,6 +268,7 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
                 groups *= 2;
             }
             stages = groups;
+            if (mode == kModeFusedFp8 && groups > 1) groups /= 2;
         }
 #ifdef IPL_TUNING_FORCE_GROUPS
         groups = IPL_TUNING_FORCE_GROUPS;

@@ -86,7 +86,9 @@ def test_plain_rms_in_place_is_accepted_by_the_plan() -> None:
     assert capi.rms_norm_plan(BASE, BASE, BASE + 8192, 2048, 3584) == "rmsnorm_staged_kernel<2, plain>"
     assert capi.rms_norm_plan(BASE + 2, BASE, BASE + 8192, 8, 3584) == "rmsnorm_rowwise_kernel<cached, plain>"
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 1, 8192) == "rmsnorm_cta_kernel<2, plain>"
-    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 8192, 8192) == "rmsnorm_stash_kernel<4, plain>"
+    # Plain RMSNorm streams through the staged ring for H > 2048, the stash kernel only below.
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 8192, 8192) == "rmsnorm_staged_kernel<2, plain>"
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 32768, 2048) == "rmsnorm_stash_kernel<4, plain>"
 
 
 def test_fp8_quant_arguments_and_plans() -> None:

@@ -52,12 +52,11 @@ def test_fused_many_rows(rows: int, hidden: int, w_off: int) -> None:
         g.assert_guards_intact()
 
 
-@pytest.mark.parametrize("rows, hidden", CASES)
+@pytest.mark.parametrize("rows, hidden", [(900, 1032), (3000, 1536), (5000, 2048)])
 @torch.inference_mode()
 def test_plain_many_rows(rows: int, hidden: int) -> None:
-    # The plain op stages only x, so the staged kernel keeps about twice the rows at once: triple
-    # the row count to stay past it.
-    rows = 3 * rows
+    # Plain RMSNorm takes this kernel only for H <= 2048 (wider rows stream through the staged
+    # ring), and past the 148 x 32 rows the staged kernel holds at once at H = 2048.
     x, _, w = _inputs(rows, hidden, rows + 5 * hidden)
     gx, go = Guarded(x.shape, 0), Guarded(x.shape, 0)
     ax = gx.load(oracle.tensor_bits(x))
