@@ -558,6 +558,9 @@ def run_ours(args, spec) -> None:
         },
         "pct_of_peak": 100.0 * achieved / peak,
         "rows_per_s": total_rows / (ms_per_step * 1e-3),
+        # The reference's own microbenchmark counts 10 B per add+RMSNorm element (the weight
+        # read for every row as well); the same time at that count, for comparison with it.
+        "gbs_at_reference_byte_count": (value * 10 / 8 if spec["op"] == "fused_add_rms_norm" else value),
         "roofline": {
             "bound": "hbm",
             "achieved": achieved,
