@@ -243,6 +243,33 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
     const int64_t row_end = p.rows * (blockIdx.x + 1) / gridDim.x;
     const int local_rows = static_cast<int>(row_end - row_begin);
 
+    // The 16-byte aligned spans of x and residual that cover a row (what the producer copies).
+    auto row_span = [&](int64_t row, uintptr_t& xbase, uintptr_t& rbase, uint32_t& bytes) {
+        const uintptr_t xa = reinterpret_cast<uintptr_t>(p.x + row * p.hidden);
+        const uintptr_t ra = kResidual ? reinterpret_cast<uintptr_t>(p.residual + row * p.hidden) : 0;
+        xbase = xa & ~static_cast<uintptr_t>(15);
+        rbase = ra & ~static_cast<uintptr_t>(15);
+        const uint32_t phase = static_cast<uint32_t>(xa - xbase) >> 1;
+        bytes = ((phase + static_cast<uint32_t>(p.hidden) + 7u) >> 3) * 16u;
+    };
+
+#ifndef IPL_TUNING_NO_PREFETCH
+    // While the previous kernel in the stream drains (this CTA may start before it completes),
+    // ask L2 for the rows this CTA copies first, so HBM is busy through the dependency wait. A
+    // prefetch only warms L2, the point where every SM's accesses meet, so it cannot return data
+    // older than what the copies after the wait see.
+    if (warp == kStagedConsumerWarps && lane == 0) {
+        const int first_round = local_rows < p.stages ? local_rows : p.stages;
+        for (int j = 0; j < first_round; ++j) {
+            uintptr_t xbase, rbase;
+            uint32_t bytes;
+            row_span(row_begin + j, xbase, rbase, bytes);
+            bulk_prefetch_l2(reinterpret_cast<const void*>(xbase), bytes);
+            if constexpr (kResidual) bulk_prefetch_l2(reinterpret_cast<const void*>(rbase), bytes);
+        }
+    }
+#endif
+
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(full_bar + 8u * s, 1);
@@ -281,14 +308,9 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
                                        kFaultEmptyBarrierTimeout)) {
                     break;
                 }
-                const int64_t row = row_begin + j;
-                const uintptr_t xa = reinterpret_cast<uintptr_t>(p.x + row * p.hidden);
-                const uintptr_t ra = kResidual ? reinterpret_cast<uintptr_t>(p.residual + row * p.hidden) : 0;
-                const uintptr_t xbase = xa & ~static_cast<uintptr_t>(15);
-                const uintptr_t rbase = ra & ~static_cast<uintptr_t>(15);
-                const uint32_t phase = static_cast<uint32_t>(xa - xbase) >> 1;
-                const uint32_t chunks = (phase + static_cast<uint32_t>(p.hidden) + 7u) >> 3;
-                const uint32_t bytes = chunks * 16u;
+                uintptr_t xbase, rbase;
+                uint32_t bytes;
+                row_span(row_begin + j, xbase, rbase, bytes);
                 const uint32_t stage = smem_base + static_cast<uint32_t>(s) * p.stage_bytes;
                 const uint32_t bar = full_bar + 8u * static_cast<uint32_t>(s);
                 mbar_arrive_expect_tx(bar, kResidual ? 2u * bytes : bytes);
@@ -589,6 +611,21 @@ constexpr int64_t kCtaRowMaxRows = IPL_TUNING_CTA_ROWS;
 constexpr int64_t kCtaRowMaxRows = 256;
 #endif
 
+// Before the dependency wait of a CTA-per-row kernel: ask L2 for the CTA's first row (16-byte
+// aligned rows, H % 8 == 0), so its loads after the wait find it there. Safe for the same reason
+// as the staged kernel's prefetch: L2 is where every SM's accesses meet.
+template <bool kResidual>
+__device__ __forceinline__ void prefetch_first_row(const WarpRowParams& p) {
+#ifndef IPL_TUNING_NO_PREFETCH
+    if (threadIdx.x == 0 && static_cast<int64_t>(blockIdx.x) < p.rows) {
+        const int64_t row = blockIdx.x;
+        const uint32_t bytes = 2u * static_cast<uint32_t>(p.hidden);
+        bulk_prefetch_l2(p.x + row * p.hidden, bytes);
+        if constexpr (kResidual) bulk_prefetch_l2(p.residual + row * p.hidden, bytes);
+    }
+#endif
+}
+
 template <int kChunks, int kMode>
 __global__ void __launch_bounds__(kCtaRowMaxThreads) rmsnorm_cta_kernel(const WarpRowParams p) {
     constexpr bool kResidual = kMode != kModePlain;
@@ -600,6 +637,7 @@ __global__ void __launch_bounds__(kCtaRowMaxThreads) rmsnorm_cta_kernel(const Wa
     const int lane = threadIdx.x % kWarpSize;
     const float hidden_f = static_cast<float>(p.hidden);
 
+    prefetch_first_row<kResidual>(p);
     // Every input (gamma and the scale included) may have been written by the previous kernel.
     grid_dependency_wait();
     grid_launch_dependents();
@@ -706,6 +744,7 @@ __global__ void __launch_bounds__(kStashMaxThreads) rmsnorm_stash_kernel(const W
     const float hidden_f = static_cast<float>(p.hidden);
     const bool weight_aligned = (reinterpret_cast<uintptr_t>(p.weight) & 15u) == 0;
 
+    prefetch_first_row<kResidual>(p);
     grid_dependency_wait();
     grid_launch_dependents();
     const float scale_inv = kFp8 ? 1.0f / *p.scale : 1.0f;

@@ -268,6 +268,12 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
         "l"(src), "r"(bytes), "r"(bar), "l"(policy)
         : "memory");
 }
+// Bulk prefetch of [src, src + bytes) into L2 (src 16-byte aligned, bytes a multiple of 16). A
+// hint only: nothing is copied anywhere a later write could leave stale, since L2 is where every
+// SM's loads and stores meet.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     uint64_t policy;
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
