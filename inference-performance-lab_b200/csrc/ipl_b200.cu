@@ -156,6 +156,10 @@ ipl_status check_rms_args(const void* x, const void* other, const void* weight, 
     return IPL_SUCCESS;
 }
 
+// Sweep builds that compare the choices below on a GPU may define IPL_TUNING_FAMILY (1 CTA per
+// row, 2 stash, 3 staged), IPL_TUNING_CTA_ROWS, IPL_TUNING_FORCE_GROUPS, IPL_TUNING_FORCE_STAGES or
+// IPL_TUNING_NO_PREFETCH; build.py defines none of them.
+//
 // Pure function of the arguments and two device limits. `other` is the residual (fused modes) or
 // the output (plain mode); either must share x's offset modulo 16 bytes for the staged kernel.
 // `out8` is the fp8 output of kModeFusedFp8, whose vector paths need 16-byte aligned rows
