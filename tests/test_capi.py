@@ -40,6 +40,52 @@ def test_library_exports_every_declared_symbol() -> None:
     assert set(declared_functions()) == set(capi.SIGNATURES)
 
 
+C_CALLER = r"""
+#include <stdio.h>
+#include <string.h>
+#include "ipl_b200.h"
+
+int main(void) {
+    const uintptr_t base = (uintptr_t)0x7F0000000000ull; /* never dereferenced */
+    void* x = (void*)base;
+    void* r = (void*)(base + ((uintptr_t)1 << 34));
+    const void* w = (const void*)(base + ((uintptr_t)1 << 35));
+    if (ipl_abi_version() != 1) return 1;
+    /* Plans are pure functions of pointers and sizes: no device needed. */
+    printf("%s\n", ipl_fused_add_rms_norm_plan(x, r, w, 2048, 3584));
+    printf("%s\n", ipl_silu_and_mul_plan(x, r, 128, 18944));
+    /* Argument errors return before any device access. */
+    ipl_status s = ipl_fused_add_rms_norm_bf16(x, r, w, 4, 3584, 0.0, NULL);
+    printf("%s: %s\n", ipl_status_string(s), ipl_last_error());
+    s = ipl_silu_and_mul_packed_bf16(x, r, 4, 18, NULL);
+    printf("%s: %s\n", ipl_status_string(s), ipl_last_error());
+    return 0;
+}
+"""
+
+
+def test_c_caller_builds_links_and_runs(tmp_path: Path) -> None:
+    """A plain C99 program includes the header and links the library, as a non-torch caller."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lib = Path(capi.library()._name)
+    source = tmp_path / "caller.c"
+    source.write_text(C_CALLER)
+    exe = tmp_path / "caller"
+    subprocess.run([cc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-I", str(HEADER.parent), str(source),
+                    "-L", str(lib.parent), "-l:" + lib.name, "-Wl,-rpath," + str(lib.parent), "-o", str(exe)],
+                   check=True, capture_output=True, text=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines()
+    assert out[0] == "rmsnorm_staged_kernel<2>"
+    assert out[1] == "silu_vector_kernel<32>"
+    assert out[2] == "IPL_ERROR_INVALID_VALUE: epsilon must be positive"
+    assert out[3].startswith("IPL_ERROR_MISALIGNED: ") and "divisible by 8" in out[3]
+
+
 def test_abi_version_and_status_strings() -> None:
     lib = capi.library()
     assert lib.ipl_abi_version() == 1
