@@ -259,6 +259,7 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
     // prefetch only warms L2, the point where every SM's accesses meet, so it cannot return data
     // older than what the copies after the wait see.
     if (warp == kStagedConsumerWarps && lane == 0) {
+        prefetch_span_l2(p.weight, 2u * static_cast<uint32_t>(p.hidden));  // gamma, copied first
         const int first_round = local_rows < p.stages ? local_rows : p.stages;
         for (int j = 0; j < first_round; ++j) {
             uintptr_t xbase, rbase;
@@ -611,6 +612,8 @@ constexpr int64_t kCtaRowMaxRows = IPL_TUNING_CTA_ROWS;
 constexpr int64_t kCtaRowMaxRows = 256;
 #endif
 
+constexpr unsigned kGammaPrefetchCtas = 148;
+
 // Before the dependency wait of a CTA-per-row kernel: ask L2 for the CTA's first row (16-byte
 // aligned rows, H % 8 == 0), so its loads after the wait find it there. Safe for the same reason
 // as the staged kernel's prefetch: L2 is where every SM's accesses meet.
@@ -622,6 +625,9 @@ __device__ __forceinline__ void prefetch_first_row(const WarpRowParams& p) {
         const uint32_t bytes = 2u * static_cast<uint32_t>(p.hidden);
         bulk_prefetch_l2(p.x + row * p.hidden, bytes);
         if constexpr (kResidual) bulk_prefetch_l2(p.residual + row * p.hidden, bytes);
+        // Gamma too (each layer of a model has its own, cold in L2 by the time it runs again);
+        // every row's pass 2 waits on it. The first CTAs are enough: later ones find it in L2.
+        if (blockIdx.x < kGammaPrefetchCtas) prefetch_span_l2(p.weight, bytes);
     }
 #endif
 }

@@ -198,7 +198,10 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
     // * up to 256 rows (decode batches): a CTA per row with the row in registers - one memory
     //   round trip, no shared-memory hand-off; 25-35 % under the others' latency;
     // * a grid of CTAs whose rows all fit in shared memory at once (at most max_stages rows per
-    //   SM): the staged kernel, which requests every row at the start;
+    //   SM): the staged kernel, which requests every row at the start, where it measured faster
+    //   than the stash kernel: 7-14 rows per SM at H 3584-6144 (at [2048, 3584] 11.3 against
+    //   11.7 us), 12-14 at H <= 2560, 7-9 at H >= 4096. With fewer rows per SM (up to 6) the
+    //   stash kernel was 9-25 % faster, and so at the other counts (4-20 %);
     // * more rows than that, or H <= 1536: a small CTA for every row (stash kernel), which
     //   streams like a copy and beat the staged ring by 2-11 % there;
     // * launches of 2^28 elements or more (2 GB of traffic, e.g. 32768 x 8192): the staged ring
@@ -212,6 +215,10 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
     const bool vector_rows = hidden % 8 == 0 && hidden <= kCtaRowMaxHidden && ((xa | oa) & 15u) == 0 && fp8_vector_ok;
     const int64_t resident_rows = static_cast<int64_t>(sm_count) * max_stages;
     const bool same_phase = (xa & 15u) == (oa & 15u);
+    const int64_t rows_per_sm = (rows + sm_count - 1) / sm_count;
+    const bool staged_resident_wins = rows <= resident_rows && same_phase && rows_per_sm >= 7 &&
+                                      !(hidden >= 4096 && rows_per_sm >= 10) &&
+                                      !(hidden <= 2560 && rows_per_sm <= 11);
 #if defined(IPL_TUNING_FAMILY)
     const int family_choice = IPL_TUNING_FAMILY;  // 1 CTA per row, 2 stash, 3 staged
 #else
@@ -220,7 +227,7 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
                               : rows * hidden >= kStagedStreamingElements        ? 3
                               : !residual && hidden > 2048 && same_phase         ? 3
                               : hidden <= 1536                                   ? 2
-                              : rows <= resident_rows && same_phase              ? 3
+                              : staged_resident_wins                             ? 3
                                                                                  : 2;
 #endif
     // Many aligned rows of moderate width: a small CTA for every row, v parked in shared memory.

@@ -274,6 +274,14 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
+// The same for any 2-byte aligned range: the 16-byte aligned span that covers [p, p + bytes)
+// (every byte of which shares a 16-byte block with a byte of the range, so it is mapped).
+__device__ __forceinline__ void prefetch_span_l2(const void* p, uint32_t bytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uintptr_t base = a & ~static_cast<uintptr_t>(15);
+    const uint32_t span = (static_cast<uint32_t>(a - base) + bytes + 15u) & ~15u;
+    bulk_prefetch_l2(reinterpret_cast<const void*>(base), span);
+}
 // Prefetch of the 128-byte line holding p into L2 (a hint, like bulk_prefetch_l2).
 __device__ __forceinline__ void prefetch_l2(const void* p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p) : "memory");
