@@ -10,7 +10,8 @@
 //
 // Kernels:
 //
-// * rmsnorm_staged_kernel - the main path. Persistent: one CTA per SM, each CTA owns a
+// * rmsnorm_staged_kernel - rows longer than 12288 elements, the fp8 op's resident grids and
+//   rows whose phase the vector kernels cannot take. Persistent: one CTA per SM, each CTA owns a
 //   contiguous block of rows. One producer thread streams whole rows of x and residual into a
 //   ring of shared-memory stages with bulk async copies (cp.async.bulk, completion on an
 //   mbarrier); consumer warps take a row at a time (a "group" of 1, 2, 4 or 8 warps per row,
@@ -29,9 +30,10 @@
 // * rmsnorm_cta_kernel - few rows (decode batches, up to 256) of 16-byte aligned rows with
 //   1024 < H <= 16384: a CTA per row, the row in registers, one memory round trip.
 //
-// * rmsnorm_stash_kernel - many 16-byte aligned rows beyond what the staged kernel holds at once
-//   (and H <= 1536): a small CTA for every row, the fp32 sum parked in shared memory between the
-//   passes. The planner (ipl_b200.cu) gives the measured crossovers.
+// * rmsnorm_stash_kernel - the main path of add+RMSNorm and RMSNorm: more than 256 16-byte
+//   aligned rows with 1024 < H <= 12288. A small CTA for every row, each thread's raw chunks
+//   held in registers across the reduction (the fp8 op parks the fp32 sum in shared memory
+//   instead). The planner (ipl_b200.cu) gives the measured crossovers.
 //
 // * rmsnorm_rowwise_kernel - the general fallback for any alignment (e.g. only one of x and
 //   residual misaligned, as in the reference's misaligned tests) and for rows too long to
@@ -720,11 +722,13 @@ __global__ void __launch_bounds__(kCtaRowMaxThreads) rmsnorm_cta_kernel(const Wa
 // ---------------------------------------------------------------------------------------------
 // Many rows of moderate width (H % 8 == 0, 16-byte aligned rows, 1024 < H <= 16384): a small CTA
 // for every row - H / 32 threads (a multiple of 32, 64..512), each owning up to four 16-byte
-// chunks whose loads it issues back to back - so a row costs one memory round trip per pass and
-// the hardware keeps many rows per SM in flight, starting the next as soon as one retires. Pass 1
-// reads x and residual, writes residual and parks the fp32 sum v in shared memory (4H bytes);
-// pass 2 reads v back, so HBM sees each byte once and registers do not hold the row across the
-// reduction.
+// chunks whose loads it issues back to back - so a row costs one memory round trip and the
+// hardware keeps many rows per SM in flight, starting the next as soon as one retires. Pass 1 reads
+// x and residual, writes residual and sums v^2; pass 2 writes the output. For the fused and plain
+// ops each thread keeps its raw x (and residual) words in registers across the reduction and
+// recomputes v (60 and 50 registers: eight or ten rows per SM, no shared memory); the fp8 op, whose
+// conversion needs registers of its own, parks v in shared memory instead (4H bytes, six rows per
+// SM). Either way HBM sees each byte once.
 
 constexpr int kStashChunks = 4;  // 16-byte chunks per thread: all of a thread's loads in flight at once
 constexpr int kStashMinThreads = 64;
@@ -737,19 +741,10 @@ __host__ __device__ constexpr uint32_t stash_smem_bytes(int hidden) { return sta
 template <int kUnroll, int kMode>
 __global__ void __launch_bounds__(kStashMaxThreads) rmsnorm_stash_kernel(const WarpRowParams p) {
     constexpr bool kResidual = kMode != kModePlain;
-    constexpr bool kFp8 = kMode == kModeFusedFp8;
-    // v in two planes: elements 0-3 of chunk k at 16k, elements 4-7 at 16 * chunks + 16k, so the
-    // 16-byte accesses of a warp's consecutive chunks hit consecutive banks (one 32-byte record
-    // per chunk made every access a 2-way bank conflict; the planes are 2-7 % faster).
-    extern __shared__ __align__(128) unsigned char smem[];
     __shared__ float partials[2][kStashMaxThreads / kWarpSize];
-    const uint32_t vbase = smem_addr(smem);
     const int threads = static_cast<int>(blockDim.x);
-    const int step = threads * kUnroll;
     const int warps = threads / kWarpSize;
     const int chunks = p.hidden >> 3;
-    const uint32_t v_step = 16u;
-    const uint32_t v_hi = static_cast<uint32_t>(chunks) * 16u;
     const int warp = threadIdx.x / kWarpSize;
     const int lane = threadIdx.x % kWarpSize;
     const float hidden_f = static_cast<float>(p.hidden);
@@ -758,19 +753,20 @@ __global__ void __launch_bounds__(kStashMaxThreads) rmsnorm_stash_kernel(const W
     prefetch_first_row<kResidual>(p);
     grid_dependency_wait();
     grid_launch_dependents();
-    const float scale_inv = kFp8 ? 1.0f / *p.scale : 1.0f;
-    const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
 
     int parity = 0;
-    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
-        const uint16_t* xr = p.x + row * p.hidden;
-        uint16_t* rr = kResidual ? p.residual + row * p.hidden : nullptr;
-        F32x2 acc = f32x2_make(0.0f, 0.0f);
-        for (int c0 = threadIdx.x; c0 < chunks; c0 += step) {
+    if constexpr (kMode != kModeFusedFp8) {
+        // Fused and plain ops: each thread's chunks (threads * kUnroll >= chunks, as planned) stay in
+        // registers as the raw bf16 words across the reduction and pass 2 recomputes v from them (the
+        // same fp32 adds, so bit for bit), so no shared memory holds the row and more rows fit per SM.
+        for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+            const uint16_t* xr = p.x + row * p.hidden;
+            uint16_t* rr = kResidual ? p.residual + row * p.hidden : nullptr;
+            F32x2 acc = f32x2_make(0.0f, 0.0f);
             U32x4 xs[kUnroll], rs[kUnroll];
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
-                const int c = c0 + u * threads;
+                const int c = threadIdx.x + u * threads;
                 if (c < chunks) {
                     xs[u] = ld_v4(xr + 8 * c);
                     if constexpr (kResidual) rs[u] = ld_v4(rr + 8 * c);
@@ -778,7 +774,7 @@ __global__ void __launch_bounds__(kStashMaxThreads) rmsnorm_stash_kernel(const W
             }
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
-                const int c = c0 + u * threads;
+                const int c = threadIdx.x + u * threads;
                 if (c < chunks) {
                     Pairs4 v;
                     if constexpr (kResidual) {
@@ -787,43 +783,99 @@ __global__ void __launch_bounds__(kStashMaxThreads) rmsnorm_stash_kernel(const W
                     } else {
                         v = chunk_widen(xs[u]);
                     }
-                    sts_pairs(vbase + v_step * c, v.v[0], v.v[1]);
-                    sts_pairs(vbase + v_step * c + v_hi, v.v[2], v.v[3]);
 #pragma unroll
                     for (int e = 0; e < 4; ++e) acc = f32x2_fma(v.v[e], v.v[e], acc);
                 }
             }
-        }
-        float acc_lo, acc_hi;
-        f32x2_split(acc, acc_lo, acc_hi);
-        const float warp_total = warp_sum(acc_lo + acc_hi);
-        if (lane == 0) partials[parity][warp] = warp_total;  // two parities: see rmsnorm_cta_kernel
-        __syncthreads();
-        float sumsq = 0.0f;
-        for (int w = 0; w < warps; ++w) sumsq += partials[parity][w];
-        parity ^= 1;
-        const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
-        const F32x2 inv2 = f32x2_make(inv, inv);
-
-        // Each thread reads back only the chunks it wrote, so the next row's pass 1 cannot
-        // overwrite v that another thread still needs.
-        for (int c0 = threadIdx.x; c0 < chunks; c0 += step) {
+            float acc_lo, acc_hi;
+            f32x2_split(acc, acc_lo, acc_hi);
+            const float warp_total = warp_sum(acc_lo + acc_hi);
+            if (lane == 0) partials[parity][warp] = warp_total;
+            __syncthreads();
+            float sumsq = 0.0f;
+            for (int w = 0; w < warps; ++w) sumsq += partials[parity][w];
+            parity ^= 1;
+            const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
+            const F32x2 inv2 = f32x2_make(inv, inv);
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
-                const int c = c0 + u * threads;
+                const int c = threadIdx.x + u * threads;
                 if (c < chunks) {
-                    Pairs4 v;
-                    lds_pairs(vbase + v_step * c, v.v[0], v.v[1]);
-                    lds_pairs(vbase + v_step * c + v_hi, v.v[2], v.v[3]);
+                    Pairs4 v = kResidual ? chunk_sum(xs[u], rs[u]) : chunk_widen(xs[u]);
                     const Pairs4 w = chunk_widen(load_weight_chunk(p.weight, c, weight_aligned));
 #pragma unroll
                     for (int e = 0; e < 4; ++e) v.v[e] = f32x2_mul(f32x2_mul(v.v[e], inv2), w.v[e]);
-                    if constexpr (kFp8) {
+                    st_v4(p.out + row * p.hidden + 8 * c, chunk_to_bf16(v));
+                }
+            }
+        }
+    } else {
+        // fp8 output: holding x and residual through the reduction costs this mode too many
+        // registers (its e4m3 conversion needs its own), so v waits in shared memory, in two
+        // planes: elements 0-3 of chunk k at 16k and elements 4-7 at 16 * chunks + 16k, so the
+        // 16-byte accesses of a warp's consecutive chunks hit consecutive banks (one 32-byte
+        // record per chunk made every access a 2-way bank conflict; 2-7 % slower).
+        extern __shared__ __align__(128) unsigned char smem[];
+        const uint32_t vbase = smem_addr(smem);
+        const int step = threads * kUnroll;
+        const uint32_t v_step = 16u;
+        const uint32_t v_hi = static_cast<uint32_t>(chunks) * 16u;
+        const float scale_inv = 1.0f / *p.scale;
+        const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
+        for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+            const uint16_t* xr = p.x + row * p.hidden;
+            uint16_t* rr = p.residual + row * p.hidden;
+            F32x2 acc = f32x2_make(0.0f, 0.0f);
+            for (int c0 = threadIdx.x; c0 < chunks; c0 += step) {
+                U32x4 xs[kUnroll], rs[kUnroll];
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) v.v[e] = f32x2_mul(v.v[e], scale_inv2);
+                for (int u = 0; u < kUnroll; ++u) {
+                    const int c = c0 + u * threads;
+                    if (c < chunks) {
+                        xs[u] = ld_v4(xr + 8 * c);
+                        rs[u] = ld_v4(rr + 8 * c);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u) {
+                    const int c = c0 + u * threads;
+                    if (c < chunks) {
+                        const Pairs4 v = chunk_sum(xs[u], rs[u]);
+                        st_v4(rr + 8 * c, chunk_to_bf16(v));
+                        sts_pairs(vbase + v_step * c, v.v[0], v.v[1]);
+                        sts_pairs(vbase + v_step * c + v_hi, v.v[2], v.v[3]);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) acc = f32x2_fma(v.v[e], v.v[e], acc);
+                    }
+                }
+            }
+            float acc_lo, acc_hi;
+            f32x2_split(acc, acc_lo, acc_hi);
+            const float warp_total = warp_sum(acc_lo + acc_hi);
+            if (lane == 0) partials[parity][warp] = warp_total;  // two parities: see rmsnorm_cta_kernel
+            __syncthreads();
+            float sumsq = 0.0f;
+            for (int w = 0; w < warps; ++w) sumsq += partials[parity][w];
+            parity ^= 1;
+            const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
+            const F32x2 inv2 = f32x2_make(inv, inv);
+
+            // Each thread reads back only the chunks it wrote, so the next row's pass 1 cannot
+            // overwrite v that another thread still needs.
+            for (int c0 = threadIdx.x; c0 < chunks; c0 += step) {
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u) {
+                    const int c = c0 + u * threads;
+                    if (c < chunks) {
+                        Pairs4 v;
+                        lds_pairs(vbase + v_step * c, v.v[0], v.v[1]);
+                        lds_pairs(vbase + v_step * c + v_hi, v.v[2], v.v[3]);
+                        const Pairs4 w = chunk_widen(load_weight_chunk(p.weight, c, weight_aligned));
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            v.v[e] = f32x2_mul(f32x2_mul(f32x2_mul(v.v[e], inv2), w.v[e]), scale_inv2);
+                        }
                         store_fp8_chunk(p.out8 + row * p.hidden + 8 * c, v, true, 8 * c, p.hidden);
-                    } else {
-                        st_v4(p.out + row * p.hidden + 8 * c, chunk_to_bf16(v));
                     }
                 }
             }

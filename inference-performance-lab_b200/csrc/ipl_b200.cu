@@ -194,24 +194,20 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         return plan;
     }
     // Aligned rows of 1024 < H <= 16384 have three kernels. The choice, from cold-L2 sweeps on
-    // B200 against each other and vLLM's kernel (257..8192 rows, H 1536..16384):
+    // B200 against each other and vLLM's kernel (257..262144 rows, H 1536..16384):
     // * up to 256 rows (decode batches): a CTA per row with the row in registers - one memory
     //   round trip, no shared-memory hand-off; 25-35 % under the others' latency;
-    // * a grid of CTAs whose rows all fit in shared memory at once (at most max_stages rows per
-    //   SM): the staged kernel, which requests every row at the start, where it measured faster
-    //   than the stash kernel: 7-14 rows per SM at H 3584-6144 (at [2048, 3584] 11.3 against
-    //   11.7 us), 12-14 at H <= 2560, 7-9 at H >= 4096. With fewer rows per SM (up to 6) the
-    //   stash kernel was 9-25 % faster, and so at the other counts (4-20 %);
-    // * more rows than that, or H <= 1536: a small CTA for every row (stash kernel), which
-    //   streams like a copy and beat the staged ring by 2-11 % there;
-    // * launches of 2^28 elements or more (2 GB of traffic, e.g. 32768 x 8192): the staged ring
-    //   again, whose per-row cost is the lower one once its start-up and drain are amortised
-    //   (97.9 % against 94.7 % of the copy peak at 262144 x 8192);
     // * H > 12288: the staged kernel at any row count (the stash kernel's 512-thread CTAs lost
     //   20-30 %);
-    // * plain RMSNorm with H > 2048: the staged kernel at any row count. With only x to read a
-    //   stash thread keeps half the bytes in flight, and the staged ring was 5-28 % faster
-    //   (80.8 against 103.4 us at 32768 x 3584).
+    // * add+RMSNorm and RMSNorm otherwise: a small CTA for every row whose threads keep their
+    //   chunks in registers (stash kernel). It streams like a copy: 10.9 against the staged
+    //   ring's 11.4 us at [2048, 3584], 2462 against 2657 us at 262144 x 8192 (106.5 % of the
+    //   copy peak), and RMSNorm at or ahead of the ring at every size. The ring was 1-4 % ahead
+    //   at three resident shapes only (2048 x 2560, 1024 x 5120, 768 x 6144);
+    // * the fp8 output, whose stash kernel parks v in shared memory (fp32, 4 B/elem): the staged
+    //   kernel when its rows all fit in shared memory at once (at most max_stages rows per SM)
+    //   at 7-14 rows per SM for H 3584-6144, 12-14 at H <= 2560, 7-9 at H >= 4096, and for
+    //   launches of 2^28 elements or more; the stash kernel elsewhere, H <= 1536 included.
     const bool vector_rows = hidden % 8 == 0 && hidden <= kCtaRowMaxHidden && ((xa | oa) & 15u) == 0 && fp8_vector_ok;
     const int64_t resident_rows = static_cast<int64_t>(sm_count) * max_stages;
     const bool same_phase = (xa & 15u) == (oa & 15u);
@@ -224,8 +220,8 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
 #else
     const int family_choice = rows <= kCtaRowMaxRows                           ? 1
                               : hidden > kStashMaxHidden                         ? 3
+                              : mode != kModeFusedFp8                            ? 2
                               : rows * hidden >= kStagedStreamingElements        ? 3
-                              : !residual && hidden > 2048 && same_phase         ? 3
                               : hidden <= 1536                                   ? 2
                               : staged_resident_wins                             ? 3
                                                                                  : 2;
@@ -240,7 +236,7 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         plan.family = RmsFamily::kStash;
         plan.chunks_per_lane = kStashChunks;
         plan.threads = static_cast<unsigned>(threads);
-        plan.smem = stash_smem_bytes(static_cast<int>(hidden));
+        plan.smem = mode == kModeFusedFp8 ? stash_smem_bytes(static_cast<int>(hidden)) : 0;  // fp8: v in shared memory
         plan.grid = static_cast<unsigned>(rows < INT_MAX ? rows : INT_MAX);
         return plan;
     }

@@ -80,7 +80,7 @@ def test_c_caller_builds_links_and_runs(tmp_path: Path) -> None:
                     "-L", str(lib.parent), "-l:" + lib.name, "-Wl,-rpath," + str(lib.parent), "-o", str(exe)],
                    check=True, capture_output=True, text=True)
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines()
-    assert out[0] == "rmsnorm_staged_kernel<2>"
+    assert out[0] == "rmsnorm_stash_kernel<4>"
     assert out[1] == "silu_vector_kernel<32>"
     assert out[2] == "IPL_ERROR_INVALID_VALUE: epsilon must be positive"
     assert out[3].startswith("IPL_ERROR_MISALIGNED: ") and "divisible by 8" in out[3]
@@ -129,12 +129,17 @@ def test_plain_rms_argument_errors(args, message) -> None:
 
 def test_plain_rms_in_place_is_accepted_by_the_plan() -> None:
     # output == input is allowed (vLLM calls it out of place, callers may reuse the buffer).
-    assert capi.rms_norm_plan(BASE, BASE, BASE + 8192, 2048, 3584) == "rmsnorm_staged_kernel<2, plain>"
+    # Each stash thread reads its chunks into registers before it writes them, so in place is safe.
+    assert capi.rms_norm_plan(BASE, BASE, BASE + 8192, 2048, 3584) == "rmsnorm_stash_kernel<4, plain>"
     assert capi.rms_norm_plan(BASE + 2, BASE, BASE + 8192, 8, 3584) == "rmsnorm_rowwise_kernel<cached, plain>"
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 1, 8192) == "rmsnorm_cta_kernel<2, plain>"
-    # Plain RMSNorm streams through the staged ring for H > 2048, the stash kernel only below.
-    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 8192, 8192) == "rmsnorm_staged_kernel<2, plain>"
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 8192, 8192) == "rmsnorm_stash_kernel<4, plain>"
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 32768, 2048) == "rmsnorm_stash_kernel<4, plain>"
+    # x and out one element off 16 bytes alike: the staged ring (vector rows need 16-byte rows).
+    assert capi.rms_norm_plan(BASE + 2, BASE + (1 << 34) + 2, BASE + 8192, 2048, 3584) == (
+        "rmsnorm_staged_kernel<2, plain>"
+    )
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 4096, 16384) == "rmsnorm_staged_kernel<4, plain>"
 
 
 def test_fp8_quant_arguments_and_plans() -> None:
@@ -195,10 +200,10 @@ def rms_plan(x_off: int, r_off: int, w_off: int, rows: int, hidden: int) -> str:
 
 
 def test_rms_plan_selection() -> None:
-    # 2048 x 3584 aligned (the bench workload): all 14 rows of a CTA in flight, 8 groups of 2
-    # warps.
-    assert rms_plan(0, 0, 0, 2048, 3584) == "rmsnorm_staged_kernel<2>"
-    # Same with x and residual both one element off 16 bytes: the same staged kernel.
+    # 2048 x 3584 aligned (the bench workload): a 128-thread CTA per row, four chunks a thread.
+    assert rms_plan(0, 0, 0, 2048, 3584) == "rmsnorm_stash_kernel<4>"
+    # x and residual both one element off 16 bytes: the staged kernel, all 14 rows of a CTA in
+    # flight, 8 groups of 2 warps.
     assert rms_plan(1, 1, 0, 2048, 3584) == "rmsnorm_staged_kernel<2>"
     # Only one of them misaligned (the reference's misaligned tests): the general row kernel.
     assert rms_plan(1, 0, 0, 8, 3584) == "rmsnorm_rowwise_kernel<cached>"
@@ -211,23 +216,17 @@ def test_rms_plan_selection() -> None:
     assert rms_plan(0, 0, 0, 5, 16384) == "rmsnorm_cta_kernel<4>"
     assert rms_plan(0, 0, 0, 5, 2048) == "rmsnorm_cta_kernel<1>"
     assert rms_plan(0, 0, 0, 64, 2056) == "rmsnorm_cta_kernel<1>"
-    # More rows, all of them in shared memory at once (up to 14 per SM at H = 3584): the staged
-    # kernel, more warps per row when a CTA has fewer rows.
-    assert rms_plan(0, 0, 0, 148 * 2, 3584) == "rmsnorm_staged_kernel<8>"
-    assert rms_plan(0, 0, 0, 148 * 4, 3584) == "rmsnorm_staged_kernel<4>"
-    assert rms_plan(0, 0, 0, 148 * 14, 3584) == "rmsnorm_staged_kernel<2>"
-    # Beyond that: a small CTA for every row (128 threads of four chunks at H = 3584).
-    assert rms_plan(0, 0, 0, 148 * 14 + 1, 3584) == "rmsnorm_stash_kernel<4>"
-    assert rms_plan(0, 0, 0, 148 * 16, 3584) == "rmsnorm_stash_kernel<4>"
-    assert rms_plan(0, 0, 0, 32768, 3584) == "rmsnorm_stash_kernel<4>"
+    # More rows, up to 12288 elements each: a small CTA for every row (128 threads of four chunks
+    # at H = 3584), at every row count, the row-sharded workload's 2^28-element shards included.
+    for rows in (257, 148 * 2, 148 * 6, 148 * 7, 148 * 14, 148 * 14 + 1, 148 * 16, 32768):
+        assert rms_plan(0, 0, 0, rows, 3584) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 148 * 14, 4096) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 148 * 14, 2048) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 16384, 8192) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 1000, 1536) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 20000, 12288) == "rmsnorm_stash_kernel<4>"
-    # From 2^28 elements a launch (the row-sharded workload's shard at 1..8 GPUs) streams through
-    # the staged ring: about 128 KB in flight, one stage per group (four 32 KB rows at H = 8192).
-    assert rms_plan(0, 0, 0, 262144, 8192) == "rmsnorm_staged_kernel<4>"
-    assert rms_plan(0, 0, 0, 32768, 8192) == "rmsnorm_staged_kernel<4>"
-    assert rms_plan(0, 0, 0, 100000, 12288) == "rmsnorm_staged_kernel<8>"
+    assert rms_plan(0, 0, 0, 262144, 8192) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 100000, 12288) == "rmsnorm_stash_kernel<4>"
     # Rows longer than 12288: the staged kernel, streaming two 64 KB stages.
     assert rms_plan(0, 0, 0, 32768, 16384) == "rmsnorm_staged_kernel<8>"
     # Short aligned rows: a warp per row.

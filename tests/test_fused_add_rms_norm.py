@@ -124,6 +124,7 @@ SWEEP = [
     (300, 3584, 0, 0, 0),
     (600, 3584, 0, 0, 0),
     (1200, 3584, 0, 0, 0),
+    (400, 16384, 0, 0, 0),
     (5, 27000, 0, 0, 0),
     (5, 40000, 0, 0, 0),
     (5, 40000, 1, 0, 0),

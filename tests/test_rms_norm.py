@@ -2,7 +2,7 @@
 vectors (its arithmetic with a zero residual) and vLLM's native rms_norm.
 
 Not an op of the reference library: it is the plain rms_norm of the vLLM IR the reference's
-plugin targets, built on the same staged kernel. Outputs within rtol = atol = 1e-2 and one bf16
+plugin targets, built on the same row kernels. Outputs within rtol = atol = 1e-2 and one bf16
 ulp of the oracle; canary guards around every tensor; in place and out of place.
 """
 

@@ -1,7 +1,7 @@
-"""GPU parity of the many-rows kernel (a small CTA for every row, the fp32 sum parked in shared
-memory; H % 8 == 0, 16-byte aligned rows, 1024 < H <= 12288, more rows than the staged kernel
-holds at once or H <= 1536) for the fused op, plain RMSNorm and the fp8-output op, against the
-oracle, with canary guards and a misaligned weight."""
+"""GPU parity of the many-rows kernel (a small CTA for every row; H % 8 == 0, 16-byte aligned rows,
+1024 < H <= 12288, more than 256 rows) for the fused op and plain RMSNorm, whose threads keep
+their chunks in registers, and the fp8-output op, which parks the fp32 sum in shared memory,
+against the oracle, with canary guards and a misaligned weight."""
 
 from __future__ import annotations
 
@@ -52,11 +52,11 @@ def test_fused_many_rows(rows: int, hidden: int, w_off: int) -> None:
         g.assert_guards_intact()
 
 
-@pytest.mark.parametrize("rows, hidden", [(900, 1032), (3000, 1536), (5000, 2048)])
+@pytest.mark.parametrize("rows, hidden", [(900, 1032), (3000, 1536), (5000, 2048), (2100, 3584), (700, 8192),
+                                         (300, 12288)])
 @torch.inference_mode()
 def test_plain_many_rows(rows: int, hidden: int) -> None:
-    # Plain RMSNorm takes this kernel only for H <= 2048 (wider rows stream through the staged
-    # ring), and past the 148 x 32 rows the staged kernel holds at once at H = 2048.
+    # Out of place, then in place (each thread reads its chunks before it writes them).
     x, _, w = _inputs(rows, hidden, rows + 5 * hidden)
     gx, go = Guarded(x.shape, 0), Guarded(x.shape, 0)
     ax = gx.load(oracle.tensor_bits(x))
