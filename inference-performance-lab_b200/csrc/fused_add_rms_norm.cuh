@@ -10,8 +10,8 @@
 //
 // Kernels:
 //
-// * rmsnorm_staged_kernel - rows longer than 12288 elements, the fp8 op's resident grids and
-//   rows whose phase the vector kernels cannot take. Persistent: one CTA per SM, each CTA owns a
+// * rmsnorm_staged_kernel - rows longer than 12288 elements and rows whose phase the vector
+//   kernels cannot take. Persistent: one CTA per SM, each CTA owns a
 //   contiguous block of rows. One producer thread streams whole rows of x and residual into a
 //   ring of shared-memory stages with bulk async copies (cp.async.bulk, completion on an
 //   mbarrier); consumer warps take a row at a time (a "group" of 1, 2, 4 or 8 warps per row,
@@ -30,10 +30,9 @@
 // * rmsnorm_cta_kernel - few rows (decode batches, up to 256) of 16-byte aligned rows with
 //   1024 < H <= 16384: a CTA per row, the row in registers, one memory round trip.
 //
-// * rmsnorm_stash_kernel - the main path of add+RMSNorm and RMSNorm: more than 256 16-byte
-//   aligned rows with 1024 < H <= 12288. A small CTA for every row, each thread's raw chunks
-//   held in registers across the reduction (the fp8 op parks the fp32 sum in shared memory
-//   instead). The planner (ipl_b200.cu) gives the measured crossovers.
+// * rmsnorm_stash_kernel - the main path of every op: more than 256 16-byte aligned rows with
+//   1024 < H <= 12288. A small CTA for every row, each thread's raw chunks held in registers
+//   across the reduction. The planner (ipl_b200.cu) gives the measured crossovers.
 //
 // * rmsnorm_rowwise_kernel - the general fallback for any alignment (e.g. only one of x and
 //   residual misaligned, as in the reference's misaligned tests) and for rows too long to
@@ -721,26 +720,26 @@ __global__ void __launch_bounds__(kCtaRowMaxThreads) rmsnorm_cta_kernel(const Wa
 
 // ---------------------------------------------------------------------------------------------
 // Many rows of moderate width (H % 8 == 0, 16-byte aligned rows, 1024 < H <= 16384): a small CTA
-// for every row - H / 32 threads (a multiple of 32, 64..512), each owning up to four 16-byte
-// chunks whose loads it issues back to back - so a row costs one memory round trip and the
-// hardware keeps many rows per SM in flight, starting the next as soon as one retires. Pass 1 reads
-// x and residual, writes residual and sums v^2; pass 2 writes the output. For the fused and plain
-// ops each thread keeps its raw x (and residual) words in registers across the reduction and
-// recomputes v (60 and 50 registers: eight or ten rows per SM, no shared memory); the fp8 op, whose
-// conversion needs registers of its own, parks v in shared memory instead (4H bytes, six rows per
-// SM). Either way HBM sees each byte once.
+// for every row - ceil(H / (8 * U)) threads rounded up to a warp (64..512), each owning up to U
+// 16-byte chunks whose loads it issues back to back - so a row costs one memory round trip and the
+// hardware keeps many rows per SM in flight, starting the next as soon as one retires. Each thread
+// keeps its raw x (and residual) words in registers across the row's reduction: pass 1 computes
+// v, writes residual and sums v^2; pass 2 recomputes v from the same words (the same fp32 adds, so
+// bit for bit) and writes the output. No shared memory holds the row, and HBM sees each byte once.
+// The launch bound holds every instance to 64 registers (fused 62, plain 56, fp8 62, plain with
+// U = 8 56; no spills): the fp8 and U = 8 instances exceed that unbounded (100 and 112) for no
+// gain in rows per SM, and 64 is what the fused op's 60 registers are allocated as anyway.
 
-constexpr int kStashChunks = 4;  // 16-byte chunks per thread: all of a thread's loads in flight at once
+constexpr int kStashChunks = 4;       // 16-byte chunks per thread: all of a thread's loads in flight at once
+constexpr int kStashWideChunks = 8;   // plain RMSNorm of long rows: twice the bytes in flight per thread
 constexpr int kStashMinThreads = 64;
 constexpr int kStashMaxThreads = 512;
 constexpr int kStashMaxHidden = 12288;  // the planner's limit; the kernel itself takes up to 16384
-constexpr int64_t kStagedStreamingElements = int64_t{1} << 28;  // from here on the staged ring streams faster
-
-__host__ __device__ constexpr uint32_t stash_smem_bytes(int hidden) { return static_cast<uint32_t>(hidden) * 4u; }
 
 template <int kUnroll, int kMode>
-__global__ void __launch_bounds__(kStashMaxThreads) rmsnorm_stash_kernel(const WarpRowParams p) {
+__global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_stash_kernel(const WarpRowParams p) {
     constexpr bool kResidual = kMode != kModePlain;
+    constexpr bool kFp8 = kMode == kModeFusedFp8;
     __shared__ float partials[2][kStashMaxThreads / kWarpSize];
     const int threads = static_cast<int>(blockDim.x);
     const int warps = threads / kWarpSize;
@@ -753,130 +752,66 @@ __global__ void __launch_bounds__(kStashMaxThreads) rmsnorm_stash_kernel(const W
     prefetch_first_row<kResidual>(p);
     grid_dependency_wait();
     grid_launch_dependents();
+    const float scale_inv = kFp8 ? 1.0f / *p.scale : 1.0f;
+    const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
 
     int parity = 0;
-    if constexpr (kMode != kModeFusedFp8) {
-        // Fused and plain ops: each thread's chunks (threads * kUnroll >= chunks, as planned) stay in
-        // registers as the raw bf16 words across the reduction and pass 2 recomputes v from them (the
-        // same fp32 adds, so bit for bit), so no shared memory holds the row and more rows fit per SM.
-        for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
-            const uint16_t* xr = p.x + row * p.hidden;
-            uint16_t* rr = kResidual ? p.residual + row * p.hidden : nullptr;
-            F32x2 acc = f32x2_make(0.0f, 0.0f);
-            U32x4 xs[kUnroll], rs[kUnroll];
+    // threads * kUnroll >= chunks, as planned: every chunk of the row belongs to one thread.
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const uint16_t* xr = p.x + row * p.hidden;
+        uint16_t* rr = kResidual ? p.residual + row * p.hidden : nullptr;
+        F32x2 acc = f32x2_make(0.0f, 0.0f);
+        U32x4 xs[kUnroll], rs[kUnroll];
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const int c = threadIdx.x + u * threads;
-                if (c < chunks) {
-                    xs[u] = ld_v4(xr + 8 * c);
-                    if constexpr (kResidual) rs[u] = ld_v4(rr + 8 * c);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const int c = threadIdx.x + u * threads;
-                if (c < chunks) {
-                    Pairs4 v;
-                    if constexpr (kResidual) {
-                        v = chunk_sum(xs[u], rs[u]);
-                        st_v4(rr + 8 * c, chunk_to_bf16(v));
-                    } else {
-                        v = chunk_widen(xs[u]);
-                    }
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) acc = f32x2_fma(v.v[e], v.v[e], acc);
-                }
-            }
-            float acc_lo, acc_hi;
-            f32x2_split(acc, acc_lo, acc_hi);
-            const float warp_total = warp_sum(acc_lo + acc_hi);
-            if (lane == 0) partials[parity][warp] = warp_total;
-            __syncthreads();
-            float sumsq = 0.0f;
-            for (int w = 0; w < warps; ++w) sumsq += partials[parity][w];
-            parity ^= 1;
-            const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
-            const F32x2 inv2 = f32x2_make(inv, inv);
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const int c = threadIdx.x + u * threads;
-                if (c < chunks) {
-                    Pairs4 v = kResidual ? chunk_sum(xs[u], rs[u]) : chunk_widen(xs[u]);
-                    const Pairs4 w = chunk_widen(load_weight_chunk(p.weight, c, weight_aligned));
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) v.v[e] = f32x2_mul(f32x2_mul(v.v[e], inv2), w.v[e]);
-                    st_v4(p.out + row * p.hidden + 8 * c, chunk_to_bf16(v));
-                }
+        for (int u = 0; u < kUnroll; ++u) {
+            const int c = threadIdx.x + u * threads;
+            if (c < chunks) {
+                xs[u] = ld_v4(xr + 8 * c);
+                if constexpr (kResidual) rs[u] = ld_v4(rr + 8 * c);
             }
         }
-    } else {
-        // fp8 output: holding x and residual through the reduction costs this mode too many
-        // registers (its e4m3 conversion needs its own), so v waits in shared memory, in two
-        // planes: elements 0-3 of chunk k at 16k and elements 4-7 at 16 * chunks + 16k, so the
-        // 16-byte accesses of a warp's consecutive chunks hit consecutive banks (one 32-byte
-        // record per chunk made every access a 2-way bank conflict; 2-7 % slower).
-        extern __shared__ __align__(128) unsigned char smem[];
-        const uint32_t vbase = smem_addr(smem);
-        const int step = threads * kUnroll;
-        const uint32_t v_step = 16u;
-        const uint32_t v_hi = static_cast<uint32_t>(chunks) * 16u;
-        const float scale_inv = 1.0f / *p.scale;
-        const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
-        for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
-            const uint16_t* xr = p.x + row * p.hidden;
-            uint16_t* rr = p.residual + row * p.hidden;
-            F32x2 acc = f32x2_make(0.0f, 0.0f);
-            for (int c0 = threadIdx.x; c0 < chunks; c0 += step) {
-                U32x4 xs[kUnroll], rs[kUnroll];
 #pragma unroll
-                for (int u = 0; u < kUnroll; ++u) {
-                    const int c = c0 + u * threads;
-                    if (c < chunks) {
-                        xs[u] = ld_v4(xr + 8 * c);
-                        rs[u] = ld_v4(rr + 8 * c);
-                    }
+        for (int u = 0; u < kUnroll; ++u) {
+            const int c = threadIdx.x + u * threads;
+            if (c < chunks) {
+                Pairs4 v;
+                if constexpr (kResidual) {
+                    v = chunk_sum(xs[u], rs[u]);
+                    st_v4(rr + 8 * c, chunk_to_bf16(v));
+                } else {
+                    v = chunk_widen(xs[u]);
                 }
 #pragma unroll
-                for (int u = 0; u < kUnroll; ++u) {
-                    const int c = c0 + u * threads;
-                    if (c < chunks) {
-                        const Pairs4 v = chunk_sum(xs[u], rs[u]);
-                        st_v4(rr + 8 * c, chunk_to_bf16(v));
-                        sts_pairs(vbase + v_step * c, v.v[0], v.v[1]);
-                        sts_pairs(vbase + v_step * c + v_hi, v.v[2], v.v[3]);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) acc = f32x2_fma(v.v[e], v.v[e], acc);
-                    }
-                }
+                for (int e = 0; e < 4; ++e) acc = f32x2_fma(v.v[e], v.v[e], acc);
             }
-            float acc_lo, acc_hi;
-            f32x2_split(acc, acc_lo, acc_hi);
-            const float warp_total = warp_sum(acc_lo + acc_hi);
-            if (lane == 0) partials[parity][warp] = warp_total;  // two parities: see rmsnorm_cta_kernel
-            __syncthreads();
-            float sumsq = 0.0f;
-            for (int w = 0; w < warps; ++w) sumsq += partials[parity][w];
-            parity ^= 1;
-            const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
-            const F32x2 inv2 = f32x2_make(inv, inv);
-
-            // Each thread reads back only the chunks it wrote, so the next row's pass 1 cannot
-            // overwrite v that another thread still needs.
-            for (int c0 = threadIdx.x; c0 < chunks; c0 += step) {
+        }
+        float acc_lo, acc_hi;
+        f32x2_split(acc, acc_lo, acc_hi);
+        const float warp_total = warp_sum(acc_lo + acc_hi);
+        if (lane == 0) partials[parity][warp] = warp_total;  // two parities: see rmsnorm_cta_kernel
+        __syncthreads();
+        float sumsq = 0.0f;
+        for (int w = 0; w < warps; ++w) sumsq += partials[parity][w];
+        parity ^= 1;
+        const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
+        const F32x2 inv2 = f32x2_make(inv, inv);
 #pragma unroll
-                for (int u = 0; u < kUnroll; ++u) {
-                    const int c = c0 + u * threads;
-                    if (c < chunks) {
-                        Pairs4 v;
-                        lds_pairs(vbase + v_step * c, v.v[0], v.v[1]);
-                        lds_pairs(vbase + v_step * c + v_hi, v.v[2], v.v[3]);
-                        const Pairs4 w = chunk_widen(load_weight_chunk(p.weight, c, weight_aligned));
+        for (int u = 0; u < kUnroll; ++u) {
+            const int c = threadIdx.x + u * threads;
+            if (c < chunks) {
+                Pairs4 v = kResidual ? chunk_sum(xs[u], rs[u]) : chunk_widen(xs[u]);
+                const Pairs4 w = chunk_widen(load_weight_chunk(p.weight, c, weight_aligned));
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            v.v[e] = f32x2_mul(f32x2_mul(f32x2_mul(v.v[e], inv2), w.v[e]), scale_inv2);
-                        }
-                        store_fp8_chunk(p.out8 + row * p.hidden + 8 * c, v, true, 8 * c, p.hidden);
-                    }
+                for (int e = 0; e < 4; ++e) v.v[e] = f32x2_mul(f32x2_mul(v.v[e], inv2), w.v[e]);
+                if constexpr (kFp8) {
+                    // The planner gives this kernel 8-byte aligned fp8 rows (H % 8 == 0).
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) v.v[e] = f32x2_mul(v.v[e], scale_inv2);
+                    const uint32_t w0 = f32x2_to_e4m3x2(v.v[0]) | (f32x2_to_e4m3x2(v.v[1]) << 16);
+                    const uint32_t w1 = f32x2_to_e4m3x2(v.v[2]) | (f32x2_to_e4m3x2(v.v[3]) << 16);
+                    st_v2(p.out8 + row * p.hidden + 8 * c, w0, w1);
+                } else {
+                    st_v4(p.out + row * p.hidden + 8 * c, chunk_to_bf16(v));
                 }
             }
         }

@@ -86,8 +86,8 @@ enum class RmsFamily { kNone, kStaged, kWarpRow, kCtaRow, kStash, kRowwiseCached
 struct RmsPlan {
     RmsFamily family = RmsFamily::kNone;
     int warps_per_row = 0;  // staged kernels: 1, 2, 4, 8 or 16
-    int chunks_per_lane = 0;  // warp- and CTA-per-row kernels: 16-byte chunks per thread (1, 2 or 4)
-    unsigned threads = 0;     // CTA-per-row kernel: block size
+    int chunks_per_lane = 0;  // warp-, CTA-per-row and stash kernels: 16-byte chunks per thread (1, 2, 4 or 8)
+    unsigned threads = 0;     // CTA-per-row and stash kernels: block size
     unsigned grid = 0;
     size_t smem = 0;
     StagedParams staged = {};
@@ -128,7 +128,9 @@ const char* rms_kernel_name(const RmsPlan& plan, int mode) {
         case RmsFamily::kCtaRow:
             while ((1 << i) < plan.chunks_per_lane) ++i;
             return kCtaNames[mode][i];
-        case RmsFamily::kStash: return kStashNames[mode];
+        case RmsFamily::kStash:
+            // Eight chunks a thread is planned for plain RMSNorm only.
+            return plan.chunks_per_lane == kStashWideChunks ? "rmsnorm_stash_kernel<8, plain>" : kStashNames[mode];
         case RmsFamily::kRowwiseCached: return kRowwiseNames[mode][0];
         case RmsFamily::kRowwiseTwoPass: return kRowwiseNames[mode][1];
     }
@@ -194,49 +196,38 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         return plan;
     }
     // Aligned rows of 1024 < H <= 16384 have three kernels. The choice, from cold-L2 sweeps on
-    // B200 against each other and vLLM's kernel (257..262144 rows, H 1536..16384):
+    // B200 against each other and vLLM's kernels (257..262144 rows, H 1536..16384):
     // * up to 256 rows (decode batches): a CTA per row with the row in registers - one memory
     //   round trip, no shared-memory hand-off; 25-35 % under the others' latency;
     // * H > 12288: the staged kernel at any row count (the stash kernel's 512-thread CTAs lost
     //   20-30 %);
-    // * add+RMSNorm and RMSNorm otherwise: a small CTA for every row whose threads keep their
-    //   chunks in registers (stash kernel). It streams like a copy: 10.9 against the staged
-    //   ring's 11.4 us at [2048, 3584], 2462 against 2657 us at 262144 x 8192 (106.5 % of the
-    //   copy peak), and RMSNorm at or ahead of the ring at every size. The ring was 1-4 % ahead
-    //   at three resident shapes only (2048 x 2560, 1024 x 5120, 768 x 6144);
-    // * the fp8 output, whose stash kernel parks v in shared memory (fp32, 4 B/elem): the staged
-    //   kernel when its rows all fit in shared memory at once (at most max_stages rows per SM)
-    //   at 7-14 rows per SM for H 3584-6144, 12-14 at H <= 2560, 7-9 at H >= 4096, and for
-    //   launches of 2^28 elements or more; the stash kernel elsewhere, H <= 1536 included.
+    // * otherwise a small CTA for every row whose threads keep their chunks in registers (stash
+    //   kernel). It streams like a copy: add+RMSNorm 10.9 against the staged ring's 11.4 us at
+    //   [2048, 3584], 2462 against 2657 us at 262144 x 8192 (106.5 % of the copy peak), RMSNorm at
+    //   or ahead of the ring at every size, the fp8 output 5-20 % ahead of the ring at all but one
+    //   of 44 shapes (2048 x 2560: 1 %). The ring was 1-4 % ahead for add+RMSNorm at three
+    //   resident shapes only (2048 x 2560, 1024 x 5120, 768 x 6144). RMSNorm of rows of 8192 and
+    //   more, 4096+ rows: eight chunks a thread (4-10 % faster there, even with vLLM's kernel at
+    //   32768 x 8192; slower on fewer or shorter rows).
     const bool vector_rows = hidden % 8 == 0 && hidden <= kCtaRowMaxHidden && ((xa | oa) & 15u) == 0 && fp8_vector_ok;
-    const int64_t resident_rows = static_cast<int64_t>(sm_count) * max_stages;
-    const bool same_phase = (xa & 15u) == (oa & 15u);
-    const int64_t rows_per_sm = (rows + sm_count - 1) / sm_count;
-    const bool staged_resident_wins = rows <= resident_rows && same_phase && rows_per_sm >= 7 &&
-                                      !(hidden >= 4096 && rows_per_sm >= 10) &&
-                                      !(hidden <= 2560 && rows_per_sm <= 11);
 #if defined(IPL_TUNING_FAMILY)
     const int family_choice = IPL_TUNING_FAMILY;  // 1 CTA per row, 2 stash, 3 staged
 #else
-    const int family_choice = rows <= kCtaRowMaxRows                           ? 1
-                              : hidden > kStashMaxHidden                         ? 3
-                              : mode != kModeFusedFp8                            ? 2
-                              : rows * hidden >= kStagedStreamingElements        ? 3
-                              : hidden <= 1536                                   ? 2
-                              : staged_resident_wins                             ? 3
-                                                                                 : 2;
+    const int family_choice = rows <= kCtaRowMaxRows ? 1 : hidden > kStashMaxHidden ? 3 : 2;
 #endif
-    // Many aligned rows of moderate width: a small CTA for every row, v parked in shared memory.
+    // Many aligned rows of moderate width: a small CTA for every row, each thread's chunks in
+    // registers (the fp8 op parks v in shared memory).
     if (vector_rows && family_choice == 2) {
         // Up to kStashChunks chunks a thread (H <= 16384 needs at most 512 threads).
+        const int per_lane = mode == kModePlain && hidden >= 8192 && rows >= 4096 ? kStashWideChunks : kStashChunks;
         const int64_t row_chunks = hidden / 8;
-        const int64_t per_warp = static_cast<int64_t>(kStashChunks) * kWarpSize;
+        const int64_t per_warp = static_cast<int64_t>(per_lane) * kWarpSize;
         int64_t threads = (row_chunks + per_warp - 1) / per_warp * kWarpSize;
         threads = threads < kStashMinThreads ? kStashMinThreads : threads;
         plan.family = RmsFamily::kStash;
-        plan.chunks_per_lane = kStashChunks;
+        plan.chunks_per_lane = per_lane;
         plan.threads = static_cast<unsigned>(threads);
-        plan.smem = mode == kModeFusedFp8 ? stash_smem_bytes(static_cast<int>(hidden)) : 0;  // fp8: v in shared memory
+        plan.smem = 0;
         plan.grid = static_cast<unsigned>(rows < INT_MAX ? rows : INT_MAX);
         return plan;
     }
@@ -310,18 +301,16 @@ const char* mode_label(int mode) {
 // Dynamic plus static shared memory above 48 KB (from H = 12288 on) needs the opt-in attribute; it
 // is set at the first launch per device and kernel instance, whatever the size.
 template <int kMode>
-ipl_status launch_stash(const RmsPlan& plan, DeviceInfo* info, cudaStream_t stream, const WarpRowParams& w) {
-    auto kernel = rmsnorm_stash_kernel<kStashChunks, kMode>;
-    const int bit = 21 + kMode;  // bits 21..23; the staged kernels use 0..20
-    if (!(info->smem_configured.load(std::memory_order_acquire) & (1u << bit))) {
-        const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                     static_cast<int>(stash_smem_bytes(kCtaRowMaxHidden)));
-        if (err != cudaSuccess) {
-            return fail(IPL_ERROR_CUDA, "%s kernel setup failed: %s", mode_label(kMode), cudaGetErrorString(err));
-        }
-        info->smem_configured.fetch_or(1u << bit, std::memory_order_acq_rel);
+ipl_status launch_stash(const RmsPlan& plan, cudaStream_t stream, const WarpRowParams& w) {
+    cudaError_t err;
+    if constexpr (kMode == kModePlain) {
+        // Eight chunks a thread is planned for plain RMSNorm only, and instantiated for it alone.
+        err = plan.chunks_per_lane == kStashWideChunks
+                  ? launch(rmsnorm_stash_kernel<kStashWideChunks, kMode>, plan.grid, plan.threads, 0, stream, w)
+                  : launch(rmsnorm_stash_kernel<kStashChunks, kMode>, plan.grid, plan.threads, 0, stream, w);
+    } else {
+        err = launch(rmsnorm_stash_kernel<kStashChunks, kMode>, plan.grid, plan.threads, 0, stream, w);
     }
-    const cudaError_t err = launch(kernel, plan.grid, plan.threads, plan.smem, stream, w);
     if (err != cudaSuccess) {
         return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
     }
@@ -431,7 +420,7 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8
             w.rows = rows;
             w.hidden = static_cast<int>(hidden);
             w.epsilon = plan.staged.epsilon;
-            return launch_stash<kMode>(plan, info, stream, w);
+            return launch_stash<kMode>(plan, stream, w);
         }
         case RmsFamily::kRowwiseCached:
         case RmsFamily::kRowwiseTwoPass: {

@@ -133,7 +133,11 @@ def test_plain_rms_in_place_is_accepted_by_the_plan() -> None:
     assert capi.rms_norm_plan(BASE, BASE, BASE + 8192, 2048, 3584) == "rmsnorm_stash_kernel<4, plain>"
     assert capi.rms_norm_plan(BASE + 2, BASE, BASE + 8192, 8, 3584) == "rmsnorm_rowwise_kernel<cached, plain>"
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 1, 8192) == "rmsnorm_cta_kernel<2, plain>"
-    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 8192, 8192) == "rmsnorm_stash_kernel<4, plain>"
+    # Rows of 8192+ elements, 4096+ of them: eight chunks a thread.
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 4095, 8192) == "rmsnorm_stash_kernel<4, plain>"
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 8192, 8192) == "rmsnorm_stash_kernel<8, plain>"
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 4096, 12288) == "rmsnorm_stash_kernel<8, plain>"
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 32768, 4096) == "rmsnorm_stash_kernel<4, plain>"
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 32768, 2048) == "rmsnorm_stash_kernel<4, plain>"
     # x and out one element off 16 bytes alike: the staged ring (vector rows need 16-byte rows).
     assert capi.rms_norm_plan(BASE + 2, BASE + (1 << 34) + 2, BASE + 8192, 2048, 3584) == (
@@ -148,7 +152,9 @@ def test_fp8_quant_arguments_and_plans() -> None:
     with pytest.raises(capi.IplError, match="epsilon must be positive"):
         capi.fused_add_rms_norm_static_fp8_quant(BASE, BASE + 4096, BASE + 8192, BASE + 12288, BASE, 4, 16, 0.0)
     plan = capi.fused_add_rms_norm_static_fp8_quant_plan
-    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 3584) == "rmsnorm_staged_kernel<2, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 3584) == "rmsnorm_stash_kernel<4, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 262144, 8192) == "rmsnorm_stash_kernel<4, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 16384) == "rmsnorm_staged_kernel<16, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 1024) == "rmsnorm_warp_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 7, 3584) == "rmsnorm_cta_kernel<1, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 9000, 4096) == "rmsnorm_stash_kernel<4, fp8>"

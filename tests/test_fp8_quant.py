@@ -44,9 +44,9 @@ def check(out8: np.ndarray, expected: np.ndarray, what: str) -> None:
 
 CASES = [
     # rows, hidden, x/residual offset (elements), output offset (bytes), scale
-    (2048, 3584, 0, 0, 0.05),     # staged kernel, whole chunks
+    (2048, 3584, 0, 0, 0.05),     # stash kernel (a CTA per row, chunks in registers)
     (7, 3584, 0, 0, 1.0),         # CTA-per-row kernel
-    (3000, 8192, 0, 0, 0.02),     # stash kernel
+    (3000, 8192, 0, 0, 0.02),     # stash kernel, 256 threads a row
     (600, 16384, 0, 0, 0.05),     # staged kernel streaming: fp8 rows get twice the warps per row
     (1000, 1024, 0, 0, 0.05),     # warp-per-row kernel
     (5, 256, 0, 0, 0.5),

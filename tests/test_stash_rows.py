@@ -1,7 +1,7 @@
-"""GPU parity of the many-rows kernel (a small CTA for every row; H % 8 == 0, 16-byte aligned rows,
-1024 < H <= 12288, more than 256 rows) for the fused op and plain RMSNorm, whose threads keep
-their chunks in registers, and the fp8-output op, which parks the fp32 sum in shared memory,
-against the oracle, with canary guards and a misaligned weight."""
+"""GPU parity of the many-rows kernel (a small CTA for every row whose threads keep their chunks
+in registers; H % 8 == 0, 16-byte aligned rows, 1024 < H <= 12288, more than 256 rows) for the
+fused op, plain RMSNorm (four chunks a thread, and eight for 4096+ rows of 8192+ elements) and
+the fp8-output op, against the oracle, with canary guards and a misaligned weight."""
 
 from __future__ import annotations
 
@@ -53,7 +53,7 @@ def test_fused_many_rows(rows: int, hidden: int, w_off: int) -> None:
 
 
 @pytest.mark.parametrize("rows, hidden", [(900, 1032), (3000, 1536), (5000, 2048), (2100, 3584), (700, 8192),
-                                         (300, 12288)])
+                                         (300, 12288), (4100, 8192), (4096, 12288)])
 @torch.inference_mode()
 def test_plain_many_rows(rows: int, hidden: int) -> None:
     # Out of place, then in place (each thread reads its chunks before it writes them).
@@ -61,7 +61,8 @@ def test_plain_many_rows(rows: int, hidden: int) -> None:
     gx, go = Guarded(x.shape, 0), Guarded(x.shape, 0)
     ax = gx.load(oracle.tensor_bits(x))
     plan = capi.rms_norm_plan(go.tensor.data_ptr(), ax.data_ptr(), w.data_ptr(), rows, hidden)
-    assert plan.startswith("rmsnorm_stash_kernel"), plan
+    wide = hidden >= 8192 and rows >= 4096
+    assert plan == ("rmsnorm_stash_kernel<8, plain>" if wide else "rmsnorm_stash_kernel<4, plain>"), plan
     torch.ops.inference_performance_lab.rms_norm(go.tensor, ax, w, 1e-6)
     assert_close_to_oracle(go.tensor, oracle.c_rms_norm(oracle.tensor_bits(x), oracle.tensor_bits(w), 1e-6),
                            f"{rows}x{hidden}")
@@ -71,7 +72,7 @@ def test_plain_many_rows(rows: int, hidden: int) -> None:
     go.assert_guards_intact()
 
 
-@pytest.mark.parametrize("rows, hidden", [(2100, 3584), (800, 8192), (1000, 1536)])
+@pytest.mark.parametrize("rows, hidden", [(2100, 3584), (800, 8192), (1000, 1536), (300, 1032), (500, 12288)])
 @torch.inference_mode()
 def test_fp8_many_rows(rows: int, hidden: int) -> None:
     x, r, w = _inputs(rows, hidden, rows + 7 * hidden)
