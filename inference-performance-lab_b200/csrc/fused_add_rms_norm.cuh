@@ -612,6 +612,13 @@ constexpr int64_t kCtaRowMaxRows = IPL_TUNING_CTA_ROWS;
 #else
 constexpr int64_t kCtaRowMaxRows = 256;
 #endif
+// Registers of the one-chunk instances (H <= 4096), held there by their launch bound, so the
+// planner can tell how many of their CTAs an SM holds at once: the bf16 ops 40, the fp8 op 64.
+constexpr int kRegistersPerSm = 65536;
+constexpr int kThreadsPerSm = 2048;
+constexpr int kCtaRowRegs = 40;
+constexpr int kCtaRowRegsFp8 = 64;
+constexpr int kCtaRowMaxResident = 8;  // CTAs an SM is counted on for one wave (at 10, 1480 x 1032 lost 13 %)
 
 constexpr unsigned kGammaPrefetchCtas = 148;
 
@@ -634,7 +641,10 @@ __device__ __forceinline__ void prefetch_first_row(const WarpRowParams& p) {
 }
 
 template <int kChunks, int kMode>
-__global__ void __launch_bounds__(kCtaRowMaxThreads) rmsnorm_cta_kernel(const WarpRowParams p) {
+__global__ void __launch_bounds__(
+    kCtaRowMaxThreads,
+    kChunks == 1 ? kRegistersPerSm / (kCtaRowMaxThreads * (kMode == kModeFusedFp8 ? kCtaRowRegsFp8 : kCtaRowRegs))
+                 : (kChunks == 2 ? 2 : 1)) rmsnorm_cta_kernel(const WarpRowParams p) {
     constexpr bool kResidual = kMode != kModePlain;
     constexpr bool kFp8 = kMode == kModeFusedFp8;
     __shared__ float partials[2][kCtaRowMaxThreads / kWarpSize];

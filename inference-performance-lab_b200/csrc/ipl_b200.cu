@@ -210,10 +210,24 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
     //   more, 4096+ rows: eight chunks a thread (4-10 % faster there, even with vLLM's kernel at
     //   32768 x 8192; slower on fewer or shorter rows).
     const bool vector_rows = hidden % 8 == 0 && hidden <= kCtaRowMaxHidden && ((xa | oa) & 15u) == 0 && fp8_vector_ok;
+    // One chunk a thread (H <= 4096): the CTA-per-row kernel also above 256 rows while every row's
+    // CTA is resident at once (3 CTAs of 448 threads an SM at H = 3584, 444 rows; 888 at 2048; the
+    // fp8 op's 64 registers: 296 at 3584), at most 8 an SM. Measured 3-29 % under the stash kernel
+    // there (e.g. 384 x 3584 3.14 against 3.43 us, 257 x 2048 2.38 against 3.14), 10-37 % over it
+    // as soon as a second wave is needed, and 13 % over it with 10 CTAs an SM at 1480 x 1032.
+    bool cta_one_wave = false;
+    if (vector_rows && hidden <= 8 * kCtaRowMaxThreads) {  // vector rows here: 1024 < H, t >= 160
+        const int64_t t = (hidden / 8 + kWarpSize - 1) / kWarpSize * kWarpSize;
+        const int64_t regs = mode == kModeFusedFp8 ? kCtaRowRegsFp8 : kCtaRowRegs;
+        int64_t per_sm = kRegistersPerSm / (t * regs);
+        if (per_sm > kThreadsPerSm / t) per_sm = kThreadsPerSm / t;
+        if (per_sm > kCtaRowMaxResident) per_sm = kCtaRowMaxResident;
+        cta_one_wave = rows <= static_cast<int64_t>(sm_count) * per_sm;
+    }
 #if defined(IPL_TUNING_FAMILY)
     const int family_choice = IPL_TUNING_FAMILY;  // 1 CTA per row, 2 stash, 3 staged
 #else
-    const int family_choice = rows <= kCtaRowMaxRows ? 1 : hidden > kStashMaxHidden ? 3 : 2;
+    const int family_choice = rows <= kCtaRowMaxRows || cta_one_wave ? 1 : hidden > kStashMaxHidden ? 3 : 2;
 #endif
     // Many aligned rows of moderate width: a small CTA for every row, each thread's chunks in
     // registers (the fp8 op parks v in shared memory).

@@ -1,0 +1,61 @@
+"""The compiled kernels' register budgets, from the ptxas report the build writes beside the library.
+
+The planner counts how many CTAs of the CTA-per-row kernel an SM holds at once from the registers
+its one-chunk instances are held to (40 for the bf16 ops, 64 for the fp8 op), and the stash
+kernel's eight rows per SM rest on its 64-register bound. A compiler that broke either, or began
+to spill, would change the measured crossovers silently; this test reads the report instead.
+"""
+
+from __future__ import annotations
+
+import re
+from pathlib import Path
+
+import pytest
+
+REPORT = (Path(__file__).resolve().parents[1] / "inference-performance-lab_b200" / "inference_performance_lab"
+          / "_native" / "libipl_b200.ptxas.txt")
+
+
+def kernel_resources() -> dict[str, tuple[int, int]]:
+    """{mangled kernel name: (registers, spill store bytes)} from the ptxas report."""
+    if not REPORT.exists():
+        pytest.skip("library not built here (no ptxas report)")
+    resources: dict[str, tuple[int, int]] = {}
+    name, spills = None, 0
+    for line in REPORT.read_text().splitlines():
+        m = re.search(r"Compiling entry function '(\w+)'", line)
+        if m:
+            name, spills = m.group(1), 0
+            continue
+        m = re.search(r"(\d+) bytes spill stores", line)
+        if m and name:
+            spills = int(m.group(1))
+            continue
+        m = re.search(r"Used (\d+) registers", line)
+        if m and name:
+            resources[name] = (int(m.group(1)), spills)
+            name = None
+    return resources
+
+
+def test_cta_row_kernel_one_chunk_registers() -> None:
+    res = kernel_resources()
+    for mode, cap in ((0, 40), (1, 40), (2, 64)):
+        regs, spills = res[f"_ZN3ipl18rmsnorm_cta_kernelILi1ELi{mode}EEEvNS_13WarpRowParamsE"]
+        assert regs <= cap and spills == 0, (mode, regs, spills)
+
+
+def test_stash_kernel_registers() -> None:
+    res = kernel_resources()
+    names = [n for n in res if n.startswith("_ZN3ipl20rmsnorm_stash_kernel")]
+    assert len(names) == 4  # <4> for each mode, <8> for plain RMSNorm
+    for n in names:
+        regs, spills = res[n]
+        assert regs <= 64 and spills == 0, (n, regs, spills)
+
+
+def test_no_kernel_spills() -> None:
+    res = kernel_resources()
+    spilling = {n: s for n, (_, s) in res.items() if s}
+    assert not spilling, spilling

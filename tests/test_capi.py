@@ -158,6 +158,9 @@ def test_fp8_quant_arguments_and_plans() -> None:
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 1024) == "rmsnorm_warp_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 7, 3584) == "rmsnorm_cta_kernel<1, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 9000, 4096) == "rmsnorm_stash_kernel<4, fp8>"
+    # The fp8 op's one-chunk CTA holds 64 registers: 2 CTAs of 448 threads an SM at H = 3584.
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 296, 3584) == "rmsnorm_cta_kernel<1, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 297, 3584) == "rmsnorm_stash_kernel<4, fp8>"
     # fp8 vector stores need 16-byte aligned rows and an 8-byte aligned output.
     assert plan(BASE + 4, BASE + 4098, BASE + (1 << 34) + 2, BASE + 12288, 2048, 3584).startswith(
         "rmsnorm_rowwise_kernel"
@@ -222,14 +225,24 @@ def test_rms_plan_selection() -> None:
     assert rms_plan(0, 0, 0, 5, 16384) == "rmsnorm_cta_kernel<4>"
     assert rms_plan(0, 0, 0, 5, 2048) == "rmsnorm_cta_kernel<1>"
     assert rms_plan(0, 0, 0, 64, 2056) == "rmsnorm_cta_kernel<1>"
+    # One chunk a thread (H <= 4096): the CTA per row also while every row's CTA is resident at once
+    # - 148 SMs x 3 CTAs of 448 threads at H = 3584, x 6 of 256 at 2048, x 8 of 192 at 1536.
+    for rows in (257, 148 * 2, 148 * 3):
+        assert rms_plan(0, 0, 0, rows, 3584) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 0, 148 * 3, 4096) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 0, 148 * 6, 2048) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 0, 148 * 8, 1536) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 0, 148 * 8, 1032) == "rmsnorm_cta_kernel<1>"  # at most 8 CTAs an SM counted
+    assert rms_plan(0, 0, 0, 148 * 8 + 1, 1032) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 257, 5120) == "rmsnorm_stash_kernel<4>"
     # More rows, up to 12288 elements each: a small CTA for every row (128 threads of four chunks
-    # at H = 3584), at every row count, the row-sharded workload's 2^28-element shards included.
-    for rows in (257, 148 * 2, 148 * 6, 148 * 7, 148 * 14, 148 * 14 + 1, 148 * 16, 32768):
+    # at H = 3584), the row-sharded workload's 2^28-element shards included.
+    for rows in (148 * 3 + 1, 148 * 6, 148 * 7, 148 * 14, 148 * 14 + 1, 148 * 16, 32768):
         assert rms_plan(0, 0, 0, rows, 3584) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 148 * 14, 4096) == "rmsnorm_stash_kernel<4>"
-    assert rms_plan(0, 0, 0, 148 * 14, 2048) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 148 * 6 + 1, 2048) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 148 * 8 + 1, 1536) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 16384, 8192) == "rmsnorm_stash_kernel<4>"
-    assert rms_plan(0, 0, 0, 1000, 1536) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 20000, 12288) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 262144, 8192) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 100000, 12288) == "rmsnorm_stash_kernel<4>"
@@ -245,6 +258,11 @@ def test_rms_plan_selection() -> None:
     assert rms_plan(0, 0, 0, 64, 1001).startswith("rmsnorm_staged_kernel")
     assert rms_plan(0, 0, 0, 64, 2052).startswith("rmsnorm_staged_kernel")
     assert rms_plan(0, 0, 0, 100000, 3580).startswith("rmsnorm_staged_kernel")
+    # Widths under one 16-byte chunk, many rows: the planner's occupancy arithmetic is skipped.
+    for hidden in range(1, 8):
+        for rows in (300, 1000, 100000):
+            assert rms_plan(0, 0, 0, rows, hidden).startswith(("rmsnorm_staged_kernel", "rmsnorm_rowwise_kernel"))
+            assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, rows, hidden) != "invalid"
     # Rows too long for two stages fall back to the two-pass row kernel.
     assert rms_plan(0, 0, 0, 64, 40000) == "rmsnorm_rowwise_kernel<two-pass>"
     assert rms_plan(1, 0, 0, 64, 40000) == "rmsnorm_rowwise_kernel<two-pass>"

@@ -1,6 +1,7 @@
 """GPU parity of the few-rows kernel (a CTA per row, values in registers; H % 8 == 0, 16-byte
-aligned rows, 1024 < H <= 16384, decode-sized row counts) for the fused op, plain RMSNorm and
-the fp8-output op, against the oracle, with canary guards and a misaligned weight."""
+aligned rows, 1024 < H <= 16384, decode-sized row counts, and with one chunk a thread as many rows
+as have their CTAs resident at once) for the fused op, plain RMSNorm and the fp8-output op,
+against the oracle, with canary guards and a misaligned weight."""
 
 from __future__ import annotations
 
@@ -23,6 +24,8 @@ def _cuda() -> None:
 HIDDEN = (1032, 1536, 2048, 3584, 4096, 5120, 8192, 12288, 16384)
 CASES = [(rows, hidden, w_off) for hidden in HIDDEN for rows in (1, 3, 64, 256) for w_off in (0, 1)
          if w_off == 0 or rows == 3]
+# One chunk a thread: up to the rows whose CTAs an SM holds at once (148 SMs x 8 / 8 / 6 / 3 / 3).
+CASES += [(1184, 1032, 0), (1184, 1536, 1), (888, 2048, 0), (444, 3584, 0), (400, 3584, 1), (444, 4096, 0)]
 
 
 def _inputs(rows: int, hidden: int, seed: int):
@@ -66,7 +69,8 @@ def test_plain_few_rows(rows: int, hidden: int, w_off: int) -> None:
         g.assert_guards_intact()
 
 
-@pytest.mark.parametrize("rows, hidden", [(1, 3584), (7, 3584), (256, 4096), (33, 16384), (5, 1032)])
+@pytest.mark.parametrize("rows, hidden", [(1, 3584), (7, 3584), (256, 4096), (33, 16384), (5, 1032), (296, 3584),
+                                         (592, 2048)])
 @torch.inference_mode()
 def test_fp8_few_rows(rows: int, hidden: int) -> None:
     x, r, w = _inputs(rows, hidden, rows + 7 * hidden)

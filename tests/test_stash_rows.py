@@ -23,8 +23,8 @@ def _cuda() -> None:
 
 # (rows, hidden): one, two and four chunks a thread, odd thread counts (H / 32 not a power of 2),
 # the largest width the planner gives this kernel.
-CASES = [(300, 1032), (1000, 1536), (3200, 2560), (2100, 3584), (2100, 4096), (1400, 5120), (800, 8192),
-         (500, 12288)]
+CASES = [(1600, 1032), (1300, 1536), (3200, 2560), (2100, 3584), (2100, 4096), (1400, 5120), (800, 8192),
+         (500, 12288), (445, 3584), (889, 2048)]
 
 
 def _inputs(rows: int, hidden: int, seed: int):
@@ -52,7 +52,7 @@ def test_fused_many_rows(rows: int, hidden: int, w_off: int) -> None:
         g.assert_guards_intact()
 
 
-@pytest.mark.parametrize("rows, hidden", [(900, 1032), (3000, 1536), (5000, 2048), (2100, 3584), (700, 8192),
+@pytest.mark.parametrize("rows, hidden", [(1600, 1032), (3000, 1536), (5000, 2048), (2100, 3584), (700, 8192),
                                          (300, 12288), (4100, 8192), (4096, 12288)])
 @torch.inference_mode()
 def test_plain_many_rows(rows: int, hidden: int) -> None:
@@ -72,7 +72,8 @@ def test_plain_many_rows(rows: int, hidden: int) -> None:
     go.assert_guards_intact()
 
 
-@pytest.mark.parametrize("rows, hidden", [(2100, 3584), (800, 8192), (1000, 1536), (300, 1032), (500, 12288)])
+@pytest.mark.parametrize("rows, hidden", [(2100, 3584), (800, 8192), (1000, 1536), (1000, 1032), (500, 12288),
+                                         (297, 3584)])
 @torch.inference_mode()
 def test_fp8_many_rows(rows: int, hidden: int) -> None:
     x, r, w = _inputs(rows, hidden, rows + 7 * hidden)
