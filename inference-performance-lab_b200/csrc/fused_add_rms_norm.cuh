@@ -744,7 +744,10 @@ constexpr int kStashChunks = 4;       // 16-byte chunks per thread: all of a thr
 constexpr int kStashWideChunks = 8;   // plain RMSNorm of long rows: twice the bytes in flight per thread
 constexpr int kStashMinThreads = 64;
 constexpr int kStashMaxThreads = 512;
-constexpr int kStashMaxHidden = 12288;  // the planner's limit; the kernel itself takes up to 16384
+constexpr int kStashMaxHidden = 16384;  // 512 threads of four chunks
+// A row the stash kernel takes beyond one wave moves at least this many bytes through HBM: below
+// it one CTA a row is held to the rate at which the GPU starts CTAs (about one a nanosecond).
+constexpr int64_t kStashMinRowBytes = 7168;
 
 template <int kUnroll, int kMode>
 __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_stash_kernel(const WarpRowParams p) {

@@ -183,8 +183,41 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
     int max_stages = room > 0 ? static_cast<int>(room / (stage_bytes + 2 * 8)) : 0;
     if (max_stages > kStagedMaxStages) max_stages = kStagedMaxStages;
 
-    // Short aligned rows: a warp per row, values in registers.
-    if (hidden % 8 == 0 && hidden <= kWarpRowMaxHidden && ((xa | oa) & 15u) == 0 && fp8_vector_ok) {
+    // Aligned rows (H % 8 == 0, 16-byte aligned, H <= 16384) have four kernels. The choice, from
+    // cold-L2 sweeps on B200 against each other and vLLM's kernels (1..262144 rows, H 128..16384):
+    // * up to 256 rows (decode batches), or with one chunk a thread (H <= 4096) as many rows as
+    //   have their CTAs resident at once: a CTA per row with the row in registers - one memory
+    //   round trip, no shared-memory hand-off. 3 CTAs of 448 threads an SM at H = 3584 (444 rows),
+    //   888 rows at 2048, the fp8 op's 64 registers: 296 at 3584; at most 8 an SM (1184 rows).
+    //   Measured 3-34 % under the other kernels there (H 128-4096; e.g. 384 x 3584 3.14 against
+    //   3.43 us, 64 x 1024 1.65 against the warp kernel's 2.41), 10-37 % over them once a second
+    //   wave is needed, and 13 % over with 10 CTAs an SM at 1480 x 1032;
+    // * more rows of H <= 1024 that move under 7 KiB each (RMSNorm up to H = 1024, add+RMSNorm up
+    //   to 768): a warp per row, eight rows a CTA. A CTA per row is held to the rate at which
+    //   the GPU starts CTAs there (about one a nanosecond: 131072 rows took ~135 us at any width
+    //   up to 512), 1.4-4x slower;
+    // * otherwise a small CTA for every row whose threads keep their chunks in registers (stash
+    //   kernel), up to H = 16384. It streams like a copy: add+RMSNorm 10.9 against the staged
+    //   ring's 11.4 us at [2048, 3584], 2462 against 2657 us at 262144 x 8192 (106.5 % of the copy
+    //   peak), 12-35 % ahead of the ring at H = 13312-16384; RMSNorm at or ahead of the ring at
+    //   every size; the fp8 output 5-20 % ahead of it at all but one of 44 shapes; 6-18 % ahead of
+    //   the warp kernel for add+RMSNorm rows of 1024 (8 KiB). The ring was 1-4 % ahead for
+    //   add+RMSNorm at three resident shapes only (2048 x 2560, 1024 x 5120, 768 x 6144). RMSNorm of
+    //   rows of 8192 and more, 4096+ rows: eight chunks a thread (4-10 % faster there, even with
+    //   vLLM's kernel at 32768 x 8192; slower on fewer or shorter rows).
+    const bool vector_rows = hidden % 8 == 0 && hidden <= kCtaRowMaxHidden && ((xa | oa) & 15u) == 0 && fp8_vector_ok;
+    bool cta_one_wave = false;
+    if (vector_rows && hidden <= 8 * kCtaRowMaxThreads) {  // one chunk a thread; t >= 32 (H >= 8)
+        const int64_t t = (hidden / 8 + kWarpSize - 1) / kWarpSize * kWarpSize;
+        const int64_t regs = mode == kModeFusedFp8 ? kCtaRowRegsFp8 : kCtaRowRegs;
+        int64_t per_sm = kRegistersPerSm / (t * regs);
+        if (per_sm > kThreadsPerSm / t) per_sm = kThreadsPerSm / t;
+        if (per_sm > kCtaRowMaxResident) per_sm = kCtaRowMaxResident;
+        cta_one_wave = rows <= static_cast<int64_t>(sm_count) * per_sm;
+    }
+    const bool few_rows = rows <= kCtaRowMaxRows || cta_one_wave;
+    const int64_t row_bytes = hidden * (mode == kModePlain ? 4 : mode == kModeFusedFp8 ? 7 : 8);  // HBM bytes
+    if (vector_rows && hidden <= kWarpRowMaxHidden && !few_rows && row_bytes < kStashMinRowBytes) {
         const int64_t per_lane = (hidden / 8 + kWarpSize - 1) / kWarpSize;
         plan.family = RmsFamily::kWarpRow;
         plan.chunks_per_lane = per_lane <= 1 ? 1 : per_lane <= 2 ? 2 : 4;
@@ -195,42 +228,12 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         plan.smem = static_cast<size_t>(hidden) * 4u;
         return plan;
     }
-    // Aligned rows of 1024 < H <= 16384 have three kernels. The choice, from cold-L2 sweeps on
-    // B200 against each other and vLLM's kernels (257..262144 rows, H 1536..16384):
-    // * up to 256 rows (decode batches): a CTA per row with the row in registers - one memory
-    //   round trip, no shared-memory hand-off; 25-35 % under the others' latency;
-    // * H > 12288: the staged kernel at any row count (the stash kernel's 512-thread CTAs lost
-    //   20-30 %);
-    // * otherwise a small CTA for every row whose threads keep their chunks in registers (stash
-    //   kernel). It streams like a copy: add+RMSNorm 10.9 against the staged ring's 11.4 us at
-    //   [2048, 3584], 2462 against 2657 us at 262144 x 8192 (106.5 % of the copy peak), RMSNorm at
-    //   or ahead of the ring at every size, the fp8 output 5-20 % ahead of the ring at all but one
-    //   of 44 shapes (2048 x 2560: 1 %). The ring was 1-4 % ahead for add+RMSNorm at three
-    //   resident shapes only (2048 x 2560, 1024 x 5120, 768 x 6144). RMSNorm of rows of 8192 and
-    //   more, 4096+ rows: eight chunks a thread (4-10 % faster there, even with vLLM's kernel at
-    //   32768 x 8192; slower on fewer or shorter rows).
-    const bool vector_rows = hidden % 8 == 0 && hidden <= kCtaRowMaxHidden && ((xa | oa) & 15u) == 0 && fp8_vector_ok;
-    // One chunk a thread (H <= 4096): the CTA-per-row kernel also above 256 rows while every row's
-    // CTA is resident at once (3 CTAs of 448 threads an SM at H = 3584, 444 rows; 888 at 2048; the
-    // fp8 op's 64 registers: 296 at 3584), at most 8 an SM. Measured 3-29 % under the stash kernel
-    // there (e.g. 384 x 3584 3.14 against 3.43 us, 257 x 2048 2.38 against 3.14), 10-37 % over it
-    // as soon as a second wave is needed, and 13 % over it with 10 CTAs an SM at 1480 x 1032.
-    bool cta_one_wave = false;
-    if (vector_rows && hidden <= 8 * kCtaRowMaxThreads) {  // vector rows here: 1024 < H, t >= 160
-        const int64_t t = (hidden / 8 + kWarpSize - 1) / kWarpSize * kWarpSize;
-        const int64_t regs = mode == kModeFusedFp8 ? kCtaRowRegsFp8 : kCtaRowRegs;
-        int64_t per_sm = kRegistersPerSm / (t * regs);
-        if (per_sm > kThreadsPerSm / t) per_sm = kThreadsPerSm / t;
-        if (per_sm > kCtaRowMaxResident) per_sm = kCtaRowMaxResident;
-        cta_one_wave = rows <= static_cast<int64_t>(sm_count) * per_sm;
-    }
 #if defined(IPL_TUNING_FAMILY)
     const int family_choice = IPL_TUNING_FAMILY;  // 1 CTA per row, 2 stash, 3 staged
 #else
-    const int family_choice = rows <= kCtaRowMaxRows || cta_one_wave ? 1 : hidden > kStashMaxHidden ? 3 : 2;
+    const int family_choice = few_rows ? 1 : hidden > kStashMaxHidden ? 3 : 2;
 #endif
-    // Many aligned rows of moderate width: a small CTA for every row, each thread's chunks in
-    // registers (the fp8 op parks v in shared memory).
+    // Many aligned rows: a small CTA for every row, each thread's chunks in registers.
     if (vector_rows && family_choice == 2) {
         // Up to kStashChunks chunks a thread (H <= 16384 needs at most 512 threads).
         const int per_lane = mode == kModePlain && hidden >= 8192 && rows >= 4096 ? kStashWideChunks : kStashChunks;

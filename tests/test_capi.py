@@ -143,7 +143,7 @@ def test_plain_rms_in_place_is_accepted_by_the_plan() -> None:
     assert capi.rms_norm_plan(BASE + 2, BASE + (1 << 34) + 2, BASE + 8192, 2048, 3584) == (
         "rmsnorm_staged_kernel<2, plain>"
     )
-    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 4096, 16384) == "rmsnorm_staged_kernel<4, plain>"
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 4096, 16384) == "rmsnorm_stash_kernel<8, plain>"
 
 
 def test_fp8_quant_arguments_and_plans() -> None:
@@ -154,8 +154,10 @@ def test_fp8_quant_arguments_and_plans() -> None:
     plan = capi.fused_add_rms_norm_static_fp8_quant_plan
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 3584) == "rmsnorm_stash_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 262144, 8192) == "rmsnorm_stash_kernel<4, fp8>"
-    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 16384) == "rmsnorm_staged_kernel<16, fp8>"
-    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 1024) == "rmsnorm_warp_kernel<4, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 16384) == "rmsnorm_stash_kernel<4, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 100000, 1024) == "rmsnorm_stash_kernel<4, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 100000, 896) == "rmsnorm_warp_kernel<4, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 1024) == "rmsnorm_stash_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 7, 3584) == "rmsnorm_cta_kernel<1, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 9000, 4096) == "rmsnorm_stash_kernel<4, fp8>"
     # The fp8 op's one-chunk CTA holds 64 registers: 2 CTAs of 448 threads an SM at H = 3584.
@@ -246,12 +248,21 @@ def test_rms_plan_selection() -> None:
     assert rms_plan(0, 0, 0, 20000, 12288) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 262144, 8192) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 100000, 12288) == "rmsnorm_stash_kernel<4>"
-    # Rows longer than 12288: the staged kernel, streaming two 64 KB stages.
-    assert rms_plan(0, 0, 0, 32768, 16384) == "rmsnorm_staged_kernel<8>"
-    # Short aligned rows: a warp per row.
-    assert rms_plan(0, 0, 0, 148 * 64, 1024) == "rmsnorm_warp_kernel<4>"
-    assert rms_plan(0, 0, 3, 5, 1000) == "rmsnorm_warp_kernel<4>"
-    assert rms_plan(0, 0, 0, 5, 256) == "rmsnorm_warp_kernel<1>"
+    # Up to 16384 elements (512 threads of four chunks); longer rows: the staged kernel.
+    assert rms_plan(0, 0, 0, 32768, 16384) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 300, 13312) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 1000, 16392) == "rmsnorm_staged_kernel<8>"
+    # Short aligned rows: a CTA per row while the CTAs are resident at once; beyond that a warp per
+    # row (eight rows a CTA) for rows that move under 7 KiB, the stash kernel for longer ones.
+    assert rms_plan(0, 0, 3, 5, 1000) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 0, 5, 256) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 0, 148 * 8, 128) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 0, 148 * 8 + 1, 128) == "rmsnorm_warp_kernel<1>"
+    assert rms_plan(0, 0, 0, 148 * 64, 512) == "rmsnorm_warp_kernel<2>"
+    assert rms_plan(0, 0, 0, 2000, 768) == "rmsnorm_warp_kernel<4>"  # 6 KiB a row
+    assert rms_plan(0, 0, 0, 2000, 896) == "rmsnorm_stash_kernel<4>"  # 7 KiB
+    assert rms_plan(0, 0, 0, 148 * 64, 1024) == "rmsnorm_stash_kernel<4>"
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 100000, 1024) == "rmsnorm_warp_kernel<4, plain>"
     assert rms_plan(1, 1, 0, 5, 1024).startswith("rmsnorm_staged_kernel")
     # Widths that are not a multiple of 8 stay on the staged kernel when x and residual share
     # their offset.

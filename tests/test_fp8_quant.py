@@ -47,8 +47,11 @@ CASES = [
     (2048, 3584, 0, 0, 0.05),     # stash kernel (a CTA per row, chunks in registers)
     (7, 3584, 0, 0, 1.0),         # CTA-per-row kernel
     (3000, 8192, 0, 0, 0.02),     # stash kernel, 256 threads a row
-    (600, 16384, 0, 0, 0.05),     # staged kernel streaming: fp8 rows get twice the warps per row
-    (1000, 1024, 0, 0, 0.05),     # warp-per-row kernel
+    (600, 16384, 0, 0, 0.05),     # stash kernel, 512 threads a row
+    (300, 16392, 0, 0, 0.05),     # staged kernel (rows longer than 16384)
+    (1000, 1024, 0, 0, 0.05),     # CTA-per-row kernel (every CTA resident at once)
+    (5000, 512, 0, 0, 0.05),      # warp-per-row kernel (3.5 KiB a row)
+    (3000, 1024, 0, 0, 0.05),     # stash kernel (7 KiB a row)
     (5, 256, 0, 0, 0.5),
     (64, 3584, 1, 0, 0.05),       # rows not 16-byte aligned: general row kernel
     (64, 3584, 0, 3, 0.05),       # output not 8-byte aligned

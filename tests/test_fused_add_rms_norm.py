@@ -125,6 +125,7 @@ SWEEP = [
     (600, 3584, 0, 0, 0),
     (1200, 3584, 0, 0, 0),
     (400, 16384, 0, 0, 0),
+    (300, 16392, 0, 0, 0),
     (5, 27000, 0, 0, 0),
     (5, 40000, 0, 0, 0),
     (5, 40000, 1, 0, 0),
