@@ -214,12 +214,12 @@ __device__ __forceinline__ Pairs4 weight_chunk(uint32_t wf_base, uint32_t plane_
     return w;
 }
 
-// kMode as above. out (bf16 modes) must share x's offset modulo 16; the fp8 mode is planned only
-// for 16-byte aligned rows with H % 8 == 0, so every fp8 chunk store is whole and 8-byte aligned.
+// kMode: the bf16 modes (the fp8 output goes to the vector kernels or the row kernel). out must
+// share x's offset modulo 16.
 template <int kWarpsPerRow, int kMode>
 __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const StagedParams p) {
     constexpr bool kResidual = kMode != kModePlain;
-    constexpr bool kFp8 = kMode == kModeFusedFp8;
+    static_assert(kMode != kModeFusedFp8, "the staged kernel writes bf16 outputs only");
     static_assert(kStagedConsumerWarps % kWarpsPerRow == 0, "groups must tile the consumer warps");
     constexpr int kGroups = kStagedConsumerWarps / kWarpsPerRow;
     constexpr int kGroupThreads = kWarpsPerRow * kWarpSize;
@@ -343,8 +343,6 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
     }
     grid_launch_dependents();
     const uint32_t wf_base = smem_base + layout.weight_f32_offset;
-    const float scale_inv = kFp8 ? 1.0f / *p.scale : 1.0f;
-    const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
 
     const int group = warp / kWarpsPerRow;
     const int warp_in_group = warp % kWarpsPerRow;
@@ -466,13 +464,7 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
                     Pairs4 v;
 #pragma unroll
                     for (int i = 0; i < 4; ++i) v.v[i] = f32x2_mul(f32x2_mul(vs[u].v[i], inv2), ws[u].v[i]);
-                    if constexpr (kFp8) {
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) v.v[i] = f32x2_mul(v.v[i], scale_inv2);
-                        store_fp8_chunk(p.out8 + row * p.hidden + first, v, full, first, p.hidden);
-                    } else {
-                        store_chunk(obase + 8 * k, chunk_to_bf16(v), full, first, p.hidden);
-                    }
+                    store_chunk(obase + 8 * k, chunk_to_bf16(v), full, first, p.hidden);
                 }
             }
         }
@@ -744,13 +736,22 @@ constexpr int kStashChunks = 4;       // 16-byte chunks per thread: all of a thr
 constexpr int kStashWideChunks = 8;   // plain RMSNorm of long rows: twice the bytes in flight per thread
 constexpr int kStashMinThreads = 64;
 constexpr int kStashMaxThreads = 512;
-constexpr int kStashMaxHidden = 16384;  // 512 threads of four chunks
+constexpr int kStashMaxHidden = 16384;      // 512 threads of four chunks
+constexpr int kStashMaxLongHidden = 32768;  // 512 threads of eight chunks
+// Add+RMSNorm and the fp8 op on rows of 16384 < H <= 20480 (up to 320 threads of eight chunks),
+// more than 256 of them: the capped instance, held to 96 registers (4-8 bytes of spills) so that
+// two CTAs share an SM - 16-25 % faster from 1024 rows than one CTA an SM at 128 registers, which
+// stays the choice from H = 24576 (two no longer fit) and for fewer rows.
+constexpr int kStashCappedThreads = 320;
+constexpr int kStashCappedMaxHidden = 8 * kStashWideChunks * kStashCappedThreads;  // 20480
 // A row the stash kernel takes beyond one wave moves at least this many bytes through HBM: below
 // it one CTA a row is held to the rate at which the GPU starts CTAs (about one a nanosecond).
 constexpr int64_t kStashMinRowBytes = 7168;
 
-template <int kUnroll, int kMode>
-__global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_stash_kernel(const WarpRowParams p) {
+template <int kUnroll, int kMode, bool kCapped = false>
+__global__ void __launch_bounds__(kCapped ? kStashCappedThreads : kStashMaxThreads,
+                                  kCapped || !(kUnroll > kStashChunks && kMode != kModePlain) ? 2 : 1)
+    rmsnorm_stash_kernel(const WarpRowParams p) {
     constexpr bool kResidual = kMode != kModePlain;
     constexpr bool kFp8 = kMode == kModeFusedFp8;
     __shared__ float partials[2][kStashMaxThreads / kWarpSize];

@@ -88,6 +88,7 @@ struct RmsPlan {
     int warps_per_row = 0;  // staged kernels: 1, 2, 4, 8 or 16
     int chunks_per_lane = 0;  // warp-, CTA-per-row and stash kernels: 16-byte chunks per thread (1, 2, 4 or 8)
     unsigned threads = 0;     // CTA-per-row and stash kernels: block size
+    bool capped = false;      // stash kernel, rows of 16384 < H <= 20480: the 96-register instance
     unsigned grid = 0;
     size_t smem = 0;
     StagedParams staged = {};
@@ -112,6 +113,8 @@ const char* rms_kernel_name(const RmsPlan& plan, int mode) {
         {"rmsnorm_cta_kernel<1, fp8>", "rmsnorm_cta_kernel<2, fp8>", "rmsnorm_cta_kernel<4, fp8>"}};
     static const char* const kStashNames[3] = {"rmsnorm_stash_kernel<4>", "rmsnorm_stash_kernel<4, plain>",
                                                "rmsnorm_stash_kernel<4, fp8>"};
+    static const char* const kStashWideNames[3] = {"rmsnorm_stash_kernel<8>", "rmsnorm_stash_kernel<8, plain>",
+                                                   "rmsnorm_stash_kernel<8, fp8>"};
     static const char* const kRowwiseNames[3][2] = {
         {"rmsnorm_rowwise_kernel<cached>", "rmsnorm_rowwise_kernel<two-pass>"},
         {"rmsnorm_rowwise_kernel<cached, plain>", "rmsnorm_rowwise_kernel<two-pass, plain>"},
@@ -130,7 +133,8 @@ const char* rms_kernel_name(const RmsPlan& plan, int mode) {
             return kCtaNames[mode][i];
         case RmsFamily::kStash:
             // Eight chunks a thread is planned for plain RMSNorm only.
-            return plan.chunks_per_lane == kStashWideChunks ? "rmsnorm_stash_kernel<8, plain>" : kStashNames[mode];
+            if (plan.capped) return mode == kModeFusedFp8 ? "rmsnorm_stash_kernel<8, fp8, capped>" : "rmsnorm_stash_kernel<8, capped>";
+            return plan.chunks_per_lane == kStashWideChunks ? kStashWideNames[mode] : kStashNames[mode];
         case RmsFamily::kRowwiseCached: return kRowwiseNames[mode][0];
         case RmsFamily::kRowwiseTwoPass: return kRowwiseNames[mode][1];
     }
@@ -233,16 +237,24 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
 #else
     const int family_choice = few_rows ? 1 : hidden > kStashMaxHidden ? 3 : 2;
 #endif
+    // Rows of 16384 < H <= 32768: the stash kernel with eight chunks a thread (up to 512 threads;
+    // add+RMSNorm and the fp8 op at 128 registers, one CTA an SM, or, up to H = 20480 and for more
+    // than 256 rows, the instance capped at 96 registers, two an SM). 2-9x the two-pass row kernel that
+    // served these rows before; against vLLM's kernel 0.8-1.03x its time.
+    const bool long_rows = hidden % 8 == 0 && hidden > kCtaRowMaxHidden && hidden <= kStashMaxLongHidden &&
+                           ((xa | oa) & 15u) == 0 && fp8_vector_ok;
     // Many aligned rows: a small CTA for every row, each thread's chunks in registers.
-    if (vector_rows && family_choice == 2) {
+    if ((vector_rows && family_choice == 2) || long_rows) {
         // Up to kStashChunks chunks a thread (H <= 16384 needs at most 512 threads).
-        const int per_lane = mode == kModePlain && hidden >= 8192 && rows >= 4096 ? kStashWideChunks : kStashChunks;
+        const int per_lane =
+            long_rows || (mode == kModePlain && hidden >= 8192 && rows >= 4096) ? kStashWideChunks : kStashChunks;
         const int64_t row_chunks = hidden / 8;
         const int64_t per_warp = static_cast<int64_t>(per_lane) * kWarpSize;
         int64_t threads = (row_chunks + per_warp - 1) / per_warp * kWarpSize;
         threads = threads < kStashMinThreads ? kStashMinThreads : threads;
         plan.family = RmsFamily::kStash;
         plan.chunks_per_lane = per_lane;
+        plan.capped = long_rows && mode != kModePlain && hidden <= kStashCappedMaxHidden && rows > kCtaRowMaxRows;
         plan.threads = static_cast<unsigned>(threads);
         plan.smem = 0;
         plan.grid = static_cast<unsigned>(rows < INT_MAX ? rows : INT_MAX);
@@ -259,7 +271,7 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         plan.grid = static_cast<unsigned>(rows < INT_MAX ? rows : INT_MAX);  // a CTA for every row
         return plan;
     }
-    if ((xa & 15u) == (oa & 15u) && max_stages >= 2 && fp8_vector_ok) {
+    if ((xa & 15u) == (oa & 15u) && max_stages >= 2 && mode != kModeFusedFp8) {
         const int grid = static_cast<int>(rows < sm_count ? rows : sm_count);
         const int64_t rows_per_cta = (rows + grid - 1) / grid;
         // Ring depth S and consumer groups G (W = 16 / G warps per row), from a sweep of both on
@@ -283,7 +295,6 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
                 groups *= 2;
             }
             stages = groups;
-            if (mode == kModeFusedFp8 && groups > 1) groups /= 2;
         }
 #ifdef IPL_TUNING_FORCE_GROUPS
         groups = IPL_TUNING_FORCE_GROUPS;
@@ -320,14 +331,18 @@ const char* mode_label(int mode) {
 template <int kMode>
 ipl_status launch_stash(const RmsPlan& plan, cudaStream_t stream, const WarpRowParams& w) {
     cudaError_t err;
-    if constexpr (kMode == kModePlain) {
-        // Eight chunks a thread is planned for plain RMSNorm only, and instantiated for it alone.
-        err = plan.chunks_per_lane == kStashWideChunks
-                  ? launch(rmsnorm_stash_kernel<kStashWideChunks, kMode>, plan.grid, plan.threads, 0, stream, w)
-                  : launch(rmsnorm_stash_kernel<kStashChunks, kMode>, plan.grid, plan.threads, 0, stream, w);
-    } else {
-        err = launch(rmsnorm_stash_kernel<kStashChunks, kMode>, plan.grid, plan.threads, 0, stream, w);
+    if constexpr (kMode != kModePlain) {
+        if (plan.capped) {
+            err = launch(rmsnorm_stash_kernel<kStashWideChunks, kMode, true>, plan.grid, plan.threads, 0, stream, w);
+            if (err != cudaSuccess) {
+                return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
+            }
+            return IPL_SUCCESS;
+        }
     }
+    err = plan.chunks_per_lane == kStashWideChunks
+              ? launch(rmsnorm_stash_kernel<kStashWideChunks, kMode>, plan.grid, plan.threads, 0, stream, w)
+              : launch(rmsnorm_stash_kernel<kStashChunks, kMode>, plan.grid, plan.threads, 0, stream, w);
     if (err != cudaSuccess) {
         return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
     }
@@ -375,12 +390,16 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8
     plan.staged.epsilon = static_cast<float>(epsilon);
     switch (plan.family) {
         case RmsFamily::kStaged:
-            switch (plan.warps_per_row) {
-                case 1: return launch_staged<1, kMode>(plan, info, stream);
-                case 2: return launch_staged<2, kMode>(plan, info, stream);
-                case 4: return launch_staged<4, kMode>(plan, info, stream);
-                case 8: return launch_staged<8, kMode>(plan, info, stream);
-                default: return launch_staged<16, kMode>(plan, info, stream);
+            if constexpr (kMode == kModeFusedFp8) {
+                return fail(IPL_ERROR_CUDA, "%s: no staged plan exists for this mode", mode_label(kMode));
+            } else {
+                switch (plan.warps_per_row) {
+                    case 1: return launch_staged<1, kMode>(plan, info, stream);
+                    case 2: return launch_staged<2, kMode>(plan, info, stream);
+                    case 4: return launch_staged<4, kMode>(plan, info, stream);
+                    case 8: return launch_staged<8, kMode>(plan, info, stream);
+                    default: return launch_staged<16, kMode>(plan, info, stream);
+                }
             }
         case RmsFamily::kWarpRow: {
             WarpRowParams w;

@@ -1,8 +1,9 @@
 """The compiled kernels' register budgets, from the ptxas report the build writes beside the library.
 
 The planner counts how many CTAs of the CTA-per-row kernel an SM holds at once from the registers
-its one-chunk instances are held to (40 for the bf16 ops, 64 for the fp8 op), and the stash
-kernel's eight rows per SM rest on its 64-register bound. A compiler that broke either, or began
+its one-chunk instances are held to (40 for the bf16 ops, 64 for the fp8 op), the stash kernel's
+eight rows per SM rest on its 64-register bound, and its capped instance for rows of up to 20480
+elements on two CTAs an SM at 96 registers. A compiler that broke either, or began
 to spill, would change the measured crossovers silently; this test reads the report instead.
 """
 
@@ -48,11 +49,16 @@ def test_cta_row_kernel_one_chunk_registers() -> None:
 
 def test_stash_kernel_registers() -> None:
     res = kernel_resources()
+    # <4, mode> and <8, plain> at 64 (eight rows an SM at four chunks); <8> of add+RMSNorm and the
+    # fp8 op at 128 (one CTA an SM), their capped instances at 96 (two CTAs of 320 threads).
+    caps = {f"_ZN3ipl20rmsnorm_stash_kernelILi{u}ELi{m}ELb{c}EEEvNS_13WarpRowParamsE": cap
+            for u, m, c, cap in ((4, 0, 0, 64), (4, 1, 0, 64), (4, 2, 0, 64), (8, 1, 0, 64),
+                                 (8, 0, 0, 128), (8, 2, 0, 128), (8, 0, 1, 96), (8, 2, 1, 96))}
     names = [n for n in res if n.startswith("_ZN3ipl20rmsnorm_stash_kernel")]
-    assert len(names) == 4  # <4> for each mode, <8> for plain RMSNorm
-    for n in names:
+    assert sorted(names) == sorted(caps)
+    for n, cap in caps.items():
         regs, spills = res[n]
-        assert regs <= 64 and spills == 0, (n, regs, spills)
+        assert regs <= cap and spills == 0, (n, regs, spills)
 
 
 def test_no_kernel_spills() -> None:

@@ -155,6 +155,10 @@ def test_fp8_quant_arguments_and_plans() -> None:
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 3584) == "rmsnorm_stash_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 262144, 8192) == "rmsnorm_stash_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 16384) == "rmsnorm_stash_kernel<4, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 18432) == "rmsnorm_stash_kernel<8, fp8, capped>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 32768) == "rmsnorm_stash_kernel<8, fp8>"
+    # The fp8 output has no staged plan: rows it cannot vectorise go to the row kernel.
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 32776).startswith("rmsnorm_rowwise_kernel")
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 100000, 1024) == "rmsnorm_stash_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 100000, 896) == "rmsnorm_warp_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 1024) == "rmsnorm_stash_kernel<4, fp8>"
@@ -251,7 +255,19 @@ def test_rms_plan_selection() -> None:
     # Up to 16384 elements (512 threads of four chunks); longer rows: the staged kernel.
     assert rms_plan(0, 0, 0, 32768, 16384) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 300, 13312) == "rmsnorm_stash_kernel<4>"
-    assert rms_plan(0, 0, 0, 1000, 16392) == "rmsnorm_staged_kernel<8>"
+    # 16384 < H <= 32768: eight chunks a thread; add+RMSNorm and the fp8 op at 96 registers (two CTAs
+    # an SM) up to 320 threads (H = 20480) for more than 256 rows, at 128 registers otherwise.
+    assert rms_plan(0, 0, 0, 1000, 16392) == "rmsnorm_stash_kernel<8, capped>"
+    assert rms_plan(0, 0, 0, 8192, 18432) == "rmsnorm_stash_kernel<8, capped>"
+    assert rms_plan(0, 0, 0, 257, 20480) == "rmsnorm_stash_kernel<8, capped>"
+    assert rms_plan(0, 0, 0, 256, 18432) == "rmsnorm_stash_kernel<8>"
+    assert rms_plan(0, 0, 0, 8192, 20488) == "rmsnorm_stash_kernel<8>"
+    assert rms_plan(0, 0, 0, 8192, 32768) == "rmsnorm_stash_kernel<8>"
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 8192, 18432) == "rmsnorm_stash_kernel<8, plain>"
+    # Longer rows, or rows off 16 bytes too long for the CTA kernels: the staged ring while two
+    # stages fit, else the two-pass row kernel.
+    assert rms_plan(0, 0, 0, 1000, 32776) == "rmsnorm_rowwise_kernel<two-pass>"
+    assert rms_plan(1, 1, 0, 1000, 16392).startswith("rmsnorm_staged_kernel")
     # Short aligned rows: a CTA per row while the CTAs are resident at once; beyond that a warp per
     # row (eight rows a CTA) for rows that move under 7 KiB, the stash kernel for longer ones.
     assert rms_plan(0, 0, 3, 5, 1000) == "rmsnorm_cta_kernel<1>"

@@ -48,7 +48,8 @@ CASES = [
     (7, 3584, 0, 0, 1.0),         # CTA-per-row kernel
     (3000, 8192, 0, 0, 0.02),     # stash kernel, 256 threads a row
     (600, 16384, 0, 0, 0.05),     # stash kernel, 512 threads a row
-    (300, 16392, 0, 0, 0.05),     # staged kernel (rows longer than 16384)
+    (300, 16392, 0, 0, 0.05),     # stash kernel, eight chunks a thread, 96 registers
+    (100, 24576, 0, 0, 0.05),     # stash kernel, eight chunks a thread, 128 registers
     (1000, 1024, 0, 0, 0.05),     # CTA-per-row kernel (every CTA resident at once)
     (5000, 512, 0, 0, 0.05),      # warp-per-row kernel (3.5 KiB a row)
     (3000, 1024, 0, 0, 0.05),     # stash kernel (7 KiB a row)

@@ -118,3 +118,41 @@ def test_graph_replay_matches_eager() -> None:
     torch.cuda.synchronize()
     assert torch.equal(gx, ex) and torch.equal(gr, er)
     del graph
+
+
+# Rows of 16384 < H <= 32768: eight chunks a thread (up to 512 threads); add+RMSNorm at 96
+# registers ("capped", two CTAs an SM) up to H = 20480 for more than 256 rows, else at 128.
+LONG = [(1000, 16392, "capped"), (300, 18432, "capped"), (257, 20480, "capped"), (256, 18432, ""),
+        (100, 24576, ""), (64, 32768, "")]
+
+
+@pytest.mark.parametrize("w_off", [0, 1])
+@pytest.mark.parametrize("rows, hidden, variant", LONG)
+@torch.inference_mode()
+def test_fused_long_rows(rows: int, hidden: int, variant: str, w_off: int) -> None:
+    x, r, w = _inputs(rows, hidden, rows + hidden + w_off)
+    gx, gr, gw = Guarded(x.shape, 0), Guarded(x.shape, 0), Guarded(w.shape, w_off)
+    ax, ar, aw = gx.load(oracle.tensor_bits(x)), gr.load(oracle.tensor_bits(r)), gw.load(oracle.tensor_bits(w))
+    plan = capi.fused_add_rms_norm_plan(ax.data_ptr(), ar.data_ptr(), aw.data_ptr(), rows, hidden)
+    assert plan == ("rmsnorm_stash_kernel<8, capped>" if variant else "rmsnorm_stash_kernel<8>"), plan
+    torch.ops.inference_performance_lab.fused_add_rms_norm(ax, ar, aw, 1e-6)
+    out, res = oracle.c_fused_add_rms_norm(oracle.tensor_bits(x), oracle.tensor_bits(r), oracle.tensor_bits(w), 1e-6)
+    assert_bits_equal(ar, res, f"{rows}x{hidden} residual")
+    assert_close_to_oracle(ax, out, f"{rows}x{hidden} output")
+    for g in (gx, gr, gw):
+        g.assert_guards_intact()
+
+
+@pytest.mark.parametrize("rows, hidden", [(1000, 18432), (300, 32768)])
+@torch.inference_mode()
+def test_plain_long_rows(rows: int, hidden: int) -> None:
+    x, _, w = _inputs(rows, hidden, rows + 9 * hidden)
+    gx, go = Guarded(x.shape, 0), Guarded(x.shape, 0)
+    ax = gx.load(oracle.tensor_bits(x))
+    plan = capi.rms_norm_plan(go.tensor.data_ptr(), ax.data_ptr(), w.data_ptr(), rows, hidden)
+    assert plan == "rmsnorm_stash_kernel<8, plain>", plan
+    torch.ops.inference_performance_lab.rms_norm(go.tensor, ax, w, 1e-6)
+    assert_close_to_oracle(go.tensor, oracle.c_rms_norm(oracle.tensor_bits(x), oracle.tensor_bits(w), 1e-6),
+                           f"{rows}x{hidden}")
+    gx.assert_guards_intact()
+    go.assert_guards_intact()
