@@ -10,8 +10,8 @@
 //
 // Kernels:
 //
-// * rmsnorm_staged_kernel - rows longer than 12288 elements and rows whose phase the vector
-//   kernels cannot take. Persistent: one CTA per SM, each CTA owns a
+// * rmsnorm_staged_kernel - rows off 16 bytes (x and residual alike) and widths that are not a
+//   multiple of 8, bf16 outputs. Persistent: one CTA per SM, each CTA owns a
 //   contiguous block of rows. One producer thread streams whole rows of x and residual into a
 //   ring of shared-memory stages with bulk async copies (cp.async.bulk, completion on an
 //   mbarrier); consumer warps take a row at a time (a "group" of 1, 2, 4 or 8 warps per row,
@@ -24,15 +24,16 @@
 //   shared-memory access is a 16-byte vector. Requires x and residual to share their offset
 //   modulo 16 bytes (they are then aligned alike in every row).
 //
-// * rmsnorm_warp_kernel - short rows (H <= 1024, H % 8 == 0, 16-byte aligned): a warp per row,
-//   values in registers, vector loads; see below.
+// * rmsnorm_warp_kernel - many short rows (H <= 1024, H % 8 == 0, 16-byte aligned) that move
+//   under 7 KiB each: a warp per row, eight rows a CTA, values in registers; see below.
 //
-// * rmsnorm_cta_kernel - few rows (decode batches, up to 256) of 16-byte aligned rows with
-//   1024 < H <= 16384: a CTA per row, the row in registers, one memory round trip.
+// * rmsnorm_cta_kernel - 16-byte aligned rows of H <= 16384, up to 256 of them (decode batches)
+//   or, with one chunk a thread, as many as have their CTAs resident at once: a CTA per row, the
+//   row in registers, one memory round trip.
 //
-// * rmsnorm_stash_kernel - the main path of every op: more than 256 16-byte aligned rows with
-//   1024 < H <= 12288. A small CTA for every row, each thread's raw chunks held in registers
-//   across the reduction. The planner (ipl_b200.cu) gives the measured crossovers.
+// * rmsnorm_stash_kernel - the main path of every op: more 16-byte aligned rows, up to
+//   H = 32768. A small CTA for every row, each thread's raw chunks held in registers across the
+//   reduction. The planner (ipl_b200.cu) gives the measured crossovers.
 //
 // * rmsnorm_rowwise_kernel - the general fallback for any alignment (e.g. only one of x and
 //   residual misaligned, as in the reference's misaligned tests) and for rows too long to

@@ -326,8 +326,7 @@ const char* mode_label(int mode) {
     return mode == kModeFused ? "fused RMSNorm" : mode == kModePlain ? "RMSNorm" : "fused RMSNorm fp8";
 }
 
-// Dynamic plus static shared memory above 48 KB (from H = 12288 on) needs the opt-in attribute; it
-// is set at the first launch per device and kernel instance, whatever the size.
+// The stash kernel uses no dynamic shared memory: each instance launches as planned.
 template <int kMode>
 ipl_status launch_stash(const RmsPlan& plan, cudaStream_t stream, const WarpRowParams& w) {
     cudaError_t err;
