@@ -191,7 +191,9 @@ class ClockSampler:
 
 
 class Dist:
-    def __init__(self, use_gpu: bool) -> None:
+    def __init__(self, use_gpu: bool, timeout_s: float = 300.0) -> None:
+        # The timeout bounds every collective: a rank that failed or left ends the others' next
+        # barrier with an error instead of a hang (300 s covers a fresh box's first torch import).
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -202,7 +204,7 @@ class Dist:
             import torch.distributed as dist
 
             backend = "nccl" if use_gpu else "gloo"
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
             self.pg = dist
 
     def barrier(self) -> None:

@@ -104,3 +104,42 @@ def test_gloo_two_rank_sharding_matches_whole_batch() -> None:
         np.testing.assert_array_equal(shard_res, res[start:stop])
         covered += stop - start
     assert covered == rows
+
+
+def _failing_rank_worker(rank: int, world: int, port: int, queue) -> None:
+    import sys
+    import time
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import bench
+
+    d = bench.Dist(use_gpu=False, timeout_s=5.0)
+    if rank == 1:
+        raise RuntimeError("rank 1 fails between steps")
+    start = time.monotonic()
+    try:
+        d.barrier()
+        queue.put(("no error", time.monotonic() - start))
+    except Exception as error:  # noqa: BLE001 - any error ends the wait, which is the point
+        queue.put((type(error).__name__, time.monotonic() - start))
+    os._exit(3)  # leave without waiting on the failed peer
+
+
+def test_failed_rank_ends_the_others_barrier() -> None:
+    """bench.py's process group: a rank that raises between steps makes the surviving rank's next
+    barrier end with an error within the group timeout, not hang (gloo, world size 2, CPU)."""
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_rank_worker, args=(rank, 2, port, queue)) for rank in range(2)]
+    for p in procs:
+        p.start()
+    outcome, waited = queue.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert outcome != "no error"
+    assert waited < 30.0
+    assert procs[1].exitcode not in (0, None) and procs[0].exitcode == 3
