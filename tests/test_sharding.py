@@ -117,6 +117,7 @@ def _failing_rank_worker(rank: int, world: int, port: int, queue) -> None:
     import bench
 
     d = bench.Dist(use_gpu=False, timeout_s=5.0)
+    d.barrier()  # step 1 completes on both ranks
     if rank == 1:
         raise RuntimeError("rank 1 fails between steps")
     start = time.monotonic()
@@ -125,6 +126,8 @@ def _failing_rank_worker(rank: int, world: int, port: int, queue) -> None:
         queue.put(("no error", time.monotonic() - start))
     except Exception as error:  # noqa: BLE001 - any error ends the wait, which is the point
         queue.put((type(error).__name__, time.monotonic() - start))
+    queue.close()
+    queue.join_thread()  # the item is in the pipe before the process ends
     os._exit(3)  # leave without waiting on the failed peer
 
 
