@@ -1,0 +1,58 @@
+"""bench.py's command-line contract, on the CPU: the reference arm's JSON line, rank handling under
+a two-rank launch, the warm-up floor, and our arm refusing to run without a GPU (no fallback)."""
+
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def run_bench(*args: str, env: dict | None = None) -> subprocess.CompletedProcess:
+    full_env = dict(os.environ)
+    full_env.update(env or {})
+    return subprocess.run([sys.executable, str(ROOT / "bench.py"), *args], cwd=ROOT, env=full_env,
+                          capture_output=True, text=True, timeout=600)
+
+
+def test_reference_arm_prints_one_contract_line() -> None:
+    out = run_bench("--impl", "reference", "--steps", "2", "--warmup", "3")
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [line for line in out.stdout.splitlines() if line.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["steps"] == 2 and d["warmup"] == 3 and d["n_gpus"] == 1
+    assert d["metric"] == "add+RMSNorm achieved HBM GB/s" and d["unit"] == "GB/s" and d["higher_is_better"]
+    assert d["value"] > 0 and "workload" in d["config"]
+    cpu = d["cpu_baseline"]
+    assert cpu["value"] == d["value"] and cpu["kind"] in ("port", "reference") and cpu["cores"] >= 1 and cpu["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_other_ranks_exit_without_work() -> None:
+    out = run_bench("--impl", "reference", "--gpus", "2", "--steps", "2", "--warmup", "3",
+                    env={"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert out.stdout.strip() == ""
+
+
+def test_warmup_below_three_is_rejected() -> None:
+    out = run_bench("--impl", "reference", "--steps", "2", "--warmup", "2")
+    assert out.returncode != 0 and "--warmup must be at least 3" in out.stderr
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the behaviour without a GPU")
+def test_our_arm_fails_loudly_without_a_gpu() -> None:
+    out = run_bench("--steps", "2", "--warmup", "3")
+    assert out.returncode != 0 and out.stdout.strip() == ""
+    assert "needs a CUDA device" in out.stderr
