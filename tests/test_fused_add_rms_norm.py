@@ -74,6 +74,24 @@ def test_custom_matches_reference(num_tokens: int) -> None:
     check(x, residual, weight, EPSILON, actual_output, actual_residual, f"T={num_tokens}")
 
 
+@pytest.mark.parametrize("num_tokens", TOKEN_COUNTS)
+@torch.inference_mode()
+def test_vllm_matches_reference(num_tokens: int) -> None:
+    """The comparison arm of the head-to-head benchmarks (vLLM's kernel) meets the same oracle, as
+    the reference's own test of it does (tests/test_fused_add_rms_norm.py:46-51 of the reference);
+    aligned tensors only."""
+    vllm_ops = pytest.importorskip("vllm._custom_ops")
+    torch.manual_seed(0)
+    x = torch.randn(num_tokens, HIDDEN_SIZE, device="cuda", dtype=torch.bfloat16)
+    residual = torch.randn_like(x)
+    weight = torch.randn(HIDDEN_SIZE, device="cuda", dtype=torch.bfloat16) * 0.1 + 1.0
+    expected_output, expected_residual = oracle.torch_fused_add_rms_norm(x.cpu(), residual.cpu(), weight.cpu(), EPSILON)
+    actual_output, actual_residual = x.clone(), residual.clone()
+    vllm_ops.fused_add_rms_norm(actual_output, actual_residual, weight, EPSILON)
+    torch.testing.assert_close(actual_residual.cpu(), expected_residual, rtol=0, atol=0)
+    torch.testing.assert_close(actual_output.cpu(), expected_output, rtol=1e-2, atol=1e-2)
+
+
 @pytest.mark.parametrize("misaligned_argument", ["x", "residual", "weight"])
 @torch.inference_mode()
 def test_custom_handles_misaligned_contiguous_tensors(misaligned_argument: str) -> None:

@@ -59,6 +59,19 @@ def test_custom_matches_reference(implementation, num_tokens: int) -> None:
     assert_close_to_oracle(actual, oracle.c_silu_and_mul(oracle.tensor_bits(x)), f"T={num_tokens}")
 
 
+@pytest.mark.parametrize("num_tokens", TOKEN_COUNTS)
+@torch.inference_mode()
+def test_vllm_matches_reference(num_tokens: int) -> None:
+    """The comparison arm of the head-to-head benchmarks (vLLM's kernel) meets the same oracle, as
+    the reference's own test of it does (tests/test_silu_and_mul.py:52-61 of the reference)."""
+    pytest.importorskip("vllm._custom_ops")
+    torch.manual_seed(0)
+    x = torch.randn((num_tokens, 2 * INTERMEDIATE_SIZE), device="cuda", dtype=torch.bfloat16)
+    output = torch.empty((num_tokens, INTERMEDIATE_SIZE), device="cuda", dtype=torch.bfloat16)
+    torch.ops._C.silu_and_mul(output, x)
+    torch.testing.assert_close(output.cpu(), oracle.torch_silu_and_mul(x.cpu()), rtol=1e-2, atol=1e-2)
+
+
 @pytest.mark.parametrize("name", SILU_CASES)
 @torch.inference_mode()
 def test_golden_vectors(name: str) -> None:
