@@ -10,8 +10,8 @@
 //
 // Kernels:
 //
-// * rmsnorm_staged_kernel - rows off 16 bytes (x and residual alike) and widths that are not a
-//   multiple of 8, bf16 outputs. Persistent: one CTA per SM, each CTA owns a
+// * rmsnorm_staged_kernel - rows off 16 bytes (x and residual alike) that the shifted kernel does
+//   not take and widths that are not a multiple of 8, bf16 outputs. Persistent: one CTA per SM, each CTA owns a
 //   contiguous block of rows. One producer thread streams whole rows of x and residual into a
 //   ring of shared-memory stages with bulk async copies (cp.async.bulk, completion on an
 //   mbarrier); consumer warps take a row at a time (a "group" of 1, 2, 4 or 8 warps per row,
@@ -34,6 +34,9 @@
 // * rmsnorm_stash_kernel - the main path of every op: more 16-byte aligned rows, up to
 //   H = 32768. A small CTA for every row, each thread's raw chunks held in registers across the
 //   reduction. The planner (ipl_b200.cu) gives the measured crossovers.
+//
+// * rmsnorm_shifted_kernel<P> - the stash kernel's scheme for many rows off 16 bytes (P elements,
+//   x and residual alike), bf16 outputs, on the aligned chunks that cover each row.
 //
 // * rmsnorm_rowwise_kernel - the general fallback for any alignment (e.g. only one of x and
 //   residual misaligned, as in the reference's misaligned tests) and for rows too long to
@@ -828,6 +831,124 @@ __global__ void __launch_bounds__(kCapped ? kStashCappedThreads : kStashMaxThrea
                 } else {
                     st_v4(p.out + row * p.hidden + 8 * c, chunk_to_bf16(v));
                 }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Many rows that start `kPhase` elements (1..7) into a 16-byte block, x and residual (or x and
+// out) alike; H % 8 == 0, so every row has that phase. The stash kernel's scheme on the H / 8 + 1
+// aligned 16-byte chunks that cover each row: the elements of the first and last chunk that lie
+// outside the row are masked out of the sum and not stored (those two chunks are stored element
+// by element; the neighbouring rows' CTAs only read them and discard them), and gamma is shifted
+// by the phase to match. The phase is a template parameter so that the shift is two aligned
+// 16-byte loads and four funnel shifts of fixed registers (with a runtime shift the kernel was
+// 2-5 % slower, with a runtime switch 5-10 %). Every loaded byte shares a 16-byte block with an
+// element of its row, so it is mapped. Bf16 outputs only.
+constexpr int kShiftedMaxHidden = 12288;       // add+RMSNorm
+constexpr int kShiftedPlainMaxHidden = 4096;   // RMSNorm: the staged ring stays ahead beyond
+
+// Gamma for aligned chunk a: weight[8a - P + k], k = 0..7, zero outside [0, hidden).
+template <int P>
+__device__ __forceinline__ U32x4 shifted_gamma_chunk(const uint16_t* weight, int a, int hidden, bool aligned) {
+    static_assert(P >= 1 && P <= 7, "phase in elements");
+    U32x4 g;
+    if (aligned) {
+        // The window of weight chunks a - 1 and a, each loaded only where it lies inside the weight.
+        const U32x4 zero = {{0u, 0u, 0u, 0u}};
+        const U32x4 lo = a > 0 ? ld_shared_ro_v4(weight + 8 * (a - 1)) : zero;
+        const U32x4 hi = 8 * a < hidden ? ld_shared_ro_v4(weight + 8 * a) : zero;
+        const uint32_t win[8] = {lo.v[0], lo.v[1], lo.v[2], lo.v[3], hi.v[0], hi.v[1], hi.v[2], hi.v[3]};
+        constexpr int s = 8 - P;  // window element that is element 8a - P
+        constexpr uint32_t bits = 16u * static_cast<uint32_t>(s & 1);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) g.v[i] = __funnelshift_r(win[s / 2 + i], win[s / 2 + i + 1], bits);
+        return g;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int j = 8 * a - P + 2 * i;
+        const uint32_t lo = (j >= 0 && j < hidden) ? weight[j] : 0u;
+        const uint32_t hi = (j + 1 >= 0 && j + 1 < hidden) ? weight[j + 1] : 0u;
+        g.v[i] = lo | (hi << 16);
+    }
+    return g;
+}
+
+template <int kMode, int kPhase>
+__global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_shifted_kernel(const WarpRowParams p) {
+    static_assert(kMode != kModeFusedFp8, "bf16 outputs only");
+    constexpr bool kResidual = kMode != kModePlain;
+    constexpr int kUnroll = kStashChunks;
+    __shared__ float partials[2][kStashMaxThreads / kWarpSize];
+    const int threads = static_cast<int>(blockDim.x);
+    const int warps = threads / kWarpSize;
+    const int chunks = (p.hidden >> 3) + 1;  // threads * kUnroll >= chunks, as planned
+    const int warp = threadIdx.x / kWarpSize;
+    const int lane = threadIdx.x % kWarpSize;
+    const float hidden_f = static_cast<float>(p.hidden);
+    const bool weight_aligned = (reinterpret_cast<uintptr_t>(p.weight) & 15u) == 0;
+
+#ifndef IPL_TUNING_NO_PREFETCH
+    if (threadIdx.x == 0 && static_cast<int64_t>(blockIdx.x) < p.rows) {
+        const int64_t row = blockIdx.x;
+        const uint32_t bytes = 2u * static_cast<uint32_t>(p.hidden);
+        prefetch_span_l2(p.x + row * p.hidden, bytes);
+        if constexpr (kResidual) prefetch_span_l2(p.residual + row * p.hidden, bytes);
+        if (blockIdx.x < kGammaPrefetchCtas) prefetch_span_l2(p.weight, bytes);
+    }
+#endif
+    grid_dependency_wait();
+    grid_launch_dependents();
+
+    int parity = 0;
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        // Chunk c covers elements 8c - kPhase .. 8c - kPhase + 7 of the row.
+        const uint16_t* xr = p.x + row * p.hidden - kPhase;
+        uint16_t* rr = kResidual ? p.residual + row * p.hidden - kPhase : nullptr;
+        uint16_t* orow = p.out + row * p.hidden - kPhase;
+        F32x2 acc = f32x2_make(0.0f, 0.0f);
+        U32x4 xs[kUnroll], rs[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int c = threadIdx.x + u * threads;
+            if (c < chunks) {
+                xs[u] = ld_v4(xr + 8 * c);
+                if constexpr (kResidual) rs[u] = ld_v4(rr + 8 * c);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int c = threadIdx.x + u * threads;
+            if (c < chunks) {
+                Pairs4 v = kResidual ? chunk_sum(xs[u], rs[u]) : chunk_widen(xs[u]);
+                const bool full = c != 0 && c != chunks - 1;
+                if (!full) mask_outside(v, 8 * c - kPhase, p.hidden);
+                if constexpr (kResidual) store_chunk(rr + 8 * c, chunk_to_bf16(v), full, 8 * c - kPhase, p.hidden);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc = f32x2_fma(v.v[e], v.v[e], acc);
+            }
+        }
+        float acc_lo, acc_hi;
+        f32x2_split(acc, acc_lo, acc_hi);
+        const float warp_total = warp_sum(acc_lo + acc_hi);
+        if (lane == 0) partials[parity][warp] = warp_total;  // two parities: see rmsnorm_cta_kernel
+        __syncthreads();
+        float sumsq = 0.0f;
+        for (int w = 0; w < warps; ++w) sumsq += partials[parity][w];
+        parity ^= 1;
+        const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
+        const F32x2 inv2 = f32x2_make(inv, inv);
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int c = threadIdx.x + u * threads;
+            if (c < chunks) {
+                Pairs4 v = kResidual ? chunk_sum(xs[u], rs[u]) : chunk_widen(xs[u]);
+                const Pairs4 w = chunk_widen(shifted_gamma_chunk<kPhase>(p.weight, c, p.hidden, weight_aligned));
+#pragma unroll
+                for (int e = 0; e < 4; ++e) v.v[e] = f32x2_mul(f32x2_mul(v.v[e], inv2), w.v[e]);
+                store_chunk(orow + 8 * c, chunk_to_bf16(v), c != 0 && c != chunks - 1, 8 * c - kPhase, p.hidden);
             }
         }
     }

@@ -81,7 +81,7 @@ cudaError_t launch(Kernel kernel, unsigned grid, unsigned block, size_t smem, cu
 // ------------------------------------------------------------------------------------------
 // add + RMSNorm / RMSNorm planning
 
-enum class RmsFamily { kNone, kStaged, kWarpRow, kCtaRow, kStash, kRowwiseCached, kRowwiseTwoPass };
+enum class RmsFamily { kNone, kStaged, kWarpRow, kCtaRow, kStash, kShifted, kRowwiseCached, kRowwiseTwoPass };
 
 struct RmsPlan {
     RmsFamily family = RmsFamily::kNone;
@@ -89,6 +89,7 @@ struct RmsPlan {
     int chunks_per_lane = 0;  // warp-, CTA-per-row and stash kernels: 16-byte chunks per thread (1, 2, 4 or 8)
     unsigned threads = 0;     // CTA-per-row and stash kernels: block size
     bool capped = false;      // stash kernel, rows of 16384 < H <= 20480: the 96-register instance
+    int phase = 0;            // shifted kernel: elements from the 16-byte block to each row
     unsigned grid = 0;
     size_t smem = 0;
     StagedParams staged = {};
@@ -132,9 +133,21 @@ const char* rms_kernel_name(const RmsPlan& plan, int mode) {
             while ((1 << i) < plan.chunks_per_lane) ++i;
             return kCtaNames[mode][i];
         case RmsFamily::kStash:
-            // Eight chunks a thread is planned for plain RMSNorm only.
+            // Eight chunks a thread: rows longer than 16384 (capped: up to 20480, more than 256
+            // rows, add+RMSNorm and fp8) and plain RMSNorm of many long rows.
             if (plan.capped) return mode == kModeFusedFp8 ? "rmsnorm_stash_kernel<8, fp8, capped>" : "rmsnorm_stash_kernel<8, capped>";
             return plan.chunks_per_lane == kStashWideChunks ? kStashWideNames[mode] : kStashNames[mode];
+        case RmsFamily::kShifted: {
+            static const char* const kShiftedNames[2][7] = {
+                {"rmsnorm_shifted_kernel<1>", "rmsnorm_shifted_kernel<2>", "rmsnorm_shifted_kernel<3>",
+                 "rmsnorm_shifted_kernel<4>", "rmsnorm_shifted_kernel<5>", "rmsnorm_shifted_kernel<6>",
+                 "rmsnorm_shifted_kernel<7>"},
+                {"rmsnorm_shifted_kernel<1, plain>", "rmsnorm_shifted_kernel<2, plain>",
+                 "rmsnorm_shifted_kernel<3, plain>", "rmsnorm_shifted_kernel<4, plain>",
+                 "rmsnorm_shifted_kernel<5, plain>", "rmsnorm_shifted_kernel<6, plain>",
+                 "rmsnorm_shifted_kernel<7, plain>"}};
+            return mode == kModeFusedFp8 ? "invalid" : kShiftedNames[mode][plan.phase - 1];
+        }
         case RmsFamily::kRowwiseCached: return kRowwiseNames[mode][0];
         case RmsFamily::kRowwiseTwoPass: return kRowwiseNames[mode][1];
     }
@@ -243,6 +256,27 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
     // served these rows before; against vLLM's kernel 0.8-1.03x its time.
     const bool long_rows = hidden % 8 == 0 && hidden > kCtaRowMaxHidden && hidden <= kStashMaxLongHidden &&
                            ((xa | oa) & 15u) == 0 && fp8_vector_ok;
+    // Many rows off 16 bytes, x and residual (or out) alike: the stash kernel's scheme on the aligned
+    // chunks that cover each row, bf16 outputs. Against the staged ring (cold, CUDA graph) 3-22 %
+    // faster for add+RMSNorm at 15 of 20 shapes of 384-16384 rows x H 2048-8192 (2048 x 3584: 11.75
+    // against 12.35 us), level at two, 7 % slower at 1024 x 4096; for RMSNorm 9-31 % faster at
+    // H = 3584 and 7-12 % slower at 8192, hence its lower limit.
+    const bool shifted_rows = hidden % 8 == 0 && hidden > kWarpRowMaxHidden && (xa & 15u) != 0 &&
+                              (xa & 15u) == (oa & 15u) && rows > kCtaRowMaxRows &&
+                              hidden <= (mode == kModeFused ? kShiftedMaxHidden
+                                         : mode == kModePlain ? kShiftedPlainMaxHidden : 0);
+    if (shifted_rows) {
+        const int64_t row_chunks = hidden / 8 + 1;
+        const int64_t per_warp = static_cast<int64_t>(kStashChunks) * kWarpSize;
+        int64_t threads = (row_chunks + per_warp - 1) / per_warp * kWarpSize;
+        threads = threads < kStashMinThreads ? kStashMinThreads : threads;
+        plan.family = RmsFamily::kShifted;
+        plan.chunks_per_lane = kStashChunks;
+        plan.phase = static_cast<int>((xa & 15u) >> 1);
+        plan.threads = static_cast<unsigned>(threads);
+        plan.grid = static_cast<unsigned>(rows < INT_MAX ? rows : INT_MAX);
+        return plan;
+    }
     // Many aligned rows: a small CTA for every row, each thread's chunks in registers.
     if ((vector_rows && family_choice == 2) || long_rows) {
         // Up to kStashChunks chunks a thread (H <= 16384 needs at most 512 threads).
@@ -456,6 +490,36 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8
             w.hidden = static_cast<int>(hidden);
             w.epsilon = plan.staged.epsilon;
             return launch_stash<kMode>(plan, stream, w);
+        }
+        case RmsFamily::kShifted: {
+            if constexpr (kMode == kModeFusedFp8) {
+                return fail(IPL_ERROR_CUDA, "%s: no shifted plan exists for this mode", mode_label(kMode));
+            } else {
+                WarpRowParams w;
+                w.x = x;
+                w.residual = residual;
+                w.out = out;
+                w.out8 = out8;
+                w.scale = scale;
+                w.weight = weight;
+                w.rows = rows;
+                w.hidden = static_cast<int>(hidden);
+                w.epsilon = plan.staged.epsilon;
+                cudaError_t err = cudaSuccess;
+                switch (plan.phase) {
+                    case 1: err = launch(rmsnorm_shifted_kernel<kMode, 1>, plan.grid, plan.threads, 0, stream, w); break;
+                    case 2: err = launch(rmsnorm_shifted_kernel<kMode, 2>, plan.grid, plan.threads, 0, stream, w); break;
+                    case 3: err = launch(rmsnorm_shifted_kernel<kMode, 3>, plan.grid, plan.threads, 0, stream, w); break;
+                    case 4: err = launch(rmsnorm_shifted_kernel<kMode, 4>, plan.grid, plan.threads, 0, stream, w); break;
+                    case 5: err = launch(rmsnorm_shifted_kernel<kMode, 5>, plan.grid, plan.threads, 0, stream, w); break;
+                    case 6: err = launch(rmsnorm_shifted_kernel<kMode, 6>, plan.grid, plan.threads, 0, stream, w); break;
+                    default: err = launch(rmsnorm_shifted_kernel<kMode, 7>, plan.grid, plan.threads, 0, stream, w); break;
+                }
+                if (err != cudaSuccess) {
+                    return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
+                }
+                return IPL_SUCCESS;
+            }
         }
         case RmsFamily::kRowwiseCached:
         case RmsFamily::kRowwiseTwoPass: {

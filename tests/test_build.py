@@ -61,6 +61,15 @@ def test_stash_kernel_registers() -> None:
         assert regs <= cap and spills == 0, (n, regs, spills)
 
 
+def test_shifted_kernel_registers() -> None:
+    res = kernel_resources()
+    names = [n for n in res if n.startswith("_ZN3ipl22rmsnorm_shifted_kernel")]
+    assert len(names) == 14  # seven phases, add+RMSNorm and RMSNorm
+    for n in names:
+        regs, spills = res[n]
+        assert regs <= 64 and spills == 0, (n, regs, spills)
+
+
 def test_no_kernel_spills() -> None:
     res = kernel_resources()
     spilling = {n: s for n, (_, s) in res.items() if s}

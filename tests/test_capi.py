@@ -139,9 +139,12 @@ def test_plain_rms_in_place_is_accepted_by_the_plan() -> None:
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 4096, 12288) == "rmsnorm_stash_kernel<8, plain>"
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 32768, 4096) == "rmsnorm_stash_kernel<4, plain>"
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 32768, 2048) == "rmsnorm_stash_kernel<4, plain>"
-    # x and out one element off 16 bytes alike: the staged ring (vector rows need 16-byte rows).
+    # x and out one element off 16 bytes alike: the shifted kernel up to H = 4096, then the staged ring.
     assert capi.rms_norm_plan(BASE + 2, BASE + (1 << 34) + 2, BASE + 8192, 2048, 3584) == (
-        "rmsnorm_staged_kernel<2, plain>"
+        "rmsnorm_shifted_kernel<1, plain>"
+    )
+    assert capi.rms_norm_plan(BASE + 2, BASE + (1 << 34) + 2, BASE + 8192, 2048, 8192).startswith(
+        "rmsnorm_staged_kernel"
     )
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 4096, 16384) == "rmsnorm_stash_kernel<8, plain>"
 
@@ -217,9 +220,16 @@ def rms_plan(x_off: int, r_off: int, w_off: int, rows: int, hidden: int) -> str:
 def test_rms_plan_selection() -> None:
     # 2048 x 3584 aligned (the bench workload): a 128-thread CTA per row, four chunks a thread.
     assert rms_plan(0, 0, 0, 2048, 3584) == "rmsnorm_stash_kernel<4>"
-    # x and residual both one element off 16 bytes: the staged kernel, all 14 rows of a CTA in
-    # flight, 8 groups of 2 warps.
-    assert rms_plan(1, 1, 0, 2048, 3584) == "rmsnorm_staged_kernel<2>"
+    # x and residual both off 16 bytes alike, more than 256 rows: the shifted kernel, one instance
+    # per phase, up to H = 12288; fewer rows or longer ones: the staged kernel.
+    for off in range(1, 8):
+        assert rms_plan(off, off, 0, 2048, 3584) == f"rmsnorm_shifted_kernel<{off}>"
+    assert rms_plan(3, 3, 1, 300, 12288) == "rmsnorm_shifted_kernel<3>"
+    assert rms_plan(1, 1, 0, 256, 3584).startswith("rmsnorm_staged_kernel")
+    assert rms_plan(1, 1, 0, 2048, 12296).startswith("rmsnorm_staged_kernel")
+    assert rms_plan(1, 1, 0, 2048, 1024).startswith("rmsnorm_staged_kernel")
+    assert capi.fused_add_rms_norm_static_fp8_quant_plan(BASE + 2, BASE + 2, BASE + (1 << 34) + 2, BASE + 8192,
+                                                          2048, 3584).startswith("rmsnorm_rowwise_kernel")
     # Only one of them misaligned (the reference's misaligned tests): the general row kernel.
     assert rms_plan(1, 0, 0, 8, 3584) == "rmsnorm_rowwise_kernel<cached>"
     assert rms_plan(0, 1, 0, 8, 3584) == "rmsnorm_rowwise_kernel<cached>"

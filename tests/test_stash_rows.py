@@ -156,3 +156,74 @@ def test_plain_long_rows(rows: int, hidden: int) -> None:
                            f"{rows}x{hidden}")
     gx.assert_guards_intact()
     go.assert_guards_intact()
+
+
+# Rows off 16 bytes, x and residual alike, every phase (H % 8 == 0): the shifted kernel works on
+# the H / 8 + 1 aligned chunks that cover each row, masks the elements of its neighbours and shifts
+# gamma by the phase (two aligned loads, or element by element for a misaligned weight).
+SHIFTED = [(300, 3584, off) for off in range(1, 8)] + [(2048, 3584, 1), (600, 1032, 5), (300, 1536, 2),
+                                                         (500, 8192, 3), (400, 12288, 7), (257, 5120, 4)]
+
+
+@pytest.mark.parametrize("w_off", [0, 3])
+@pytest.mark.parametrize("rows, hidden, off", SHIFTED)
+@torch.inference_mode()
+def test_fused_shifted_rows(rows: int, hidden: int, off: int, w_off: int) -> None:
+    x, r, w = _inputs(rows, hidden, 7 * rows + hidden + 11 * off + w_off)
+    gx, gr, gw = Guarded(x.shape, off), Guarded(x.shape, off), Guarded(w.shape, w_off)
+    ax, ar, aw = gx.load(oracle.tensor_bits(x)), gr.load(oracle.tensor_bits(r)), gw.load(oracle.tensor_bits(w))
+    plan = capi.fused_add_rms_norm_plan(ax.data_ptr(), ar.data_ptr(), aw.data_ptr(), rows, hidden)
+    assert plan == f"rmsnorm_shifted_kernel<{off}>", plan
+    torch.ops.inference_performance_lab.fused_add_rms_norm(ax, ar, aw, 1e-6)
+    out, res = oracle.c_fused_add_rms_norm(oracle.tensor_bits(x), oracle.tensor_bits(r), oracle.tensor_bits(w), 1e-6)
+    assert_bits_equal(ar, res, f"{rows}x{hidden}+{off} residual")
+    assert_close_to_oracle(ax, out, f"{rows}x{hidden}+{off} output")
+    for g in (gx, gr, gw):
+        g.assert_guards_intact()
+
+
+@pytest.mark.parametrize("rows, hidden, off", [(300, 3584, 1), (700, 4096, 6), (400, 2048, 3), (2000, 1536, 2)])
+@torch.inference_mode()
+def test_plain_shifted_rows(rows: int, hidden: int, off: int) -> None:
+    x, _, w = _inputs(rows, hidden, 3 * rows + hidden + off)
+    gx, go = Guarded(x.shape, off), Guarded(x.shape, off)
+    ax = gx.load(oracle.tensor_bits(x))
+    plan = capi.rms_norm_plan(go.tensor.data_ptr(), ax.data_ptr(), w.data_ptr(), rows, hidden)
+    assert plan == f"rmsnorm_shifted_kernel<{off}, plain>", plan
+    torch.ops.inference_performance_lab.rms_norm(go.tensor, ax, w, 1e-6)
+    assert_close_to_oracle(go.tensor, oracle.c_rms_norm(oracle.tensor_bits(x), oracle.tensor_bits(w), 1e-6),
+                           f"{rows}x{hidden}+{off}")
+    torch.ops.inference_performance_lab.rms_norm(ax, ax, w, 1e-6)  # in place
+    assert torch.equal(ax, go.tensor)
+    gx.assert_guards_intact()
+    go.assert_guards_intact()
+
+
+@torch.inference_mode()
+def test_shifted_graph_replay_matches_eager() -> None:
+    rows, hidden, off = 2100, 3584, 3
+    x, r, w = _inputs(rows, hidden, 17)
+    gx, gr = Guarded(x.shape, off), Guarded(x.shape, off)
+    ex, er = gx.load(oracle.tensor_bits(x)), gr.load(oracle.tensor_bits(r))
+    assert capi.fused_add_rms_norm_plan(ex.data_ptr(), er.data_ptr(), w.data_ptr(), rows, hidden) == (
+        "rmsnorm_shifted_kernel<3>"
+    )
+    for _ in range(2):
+        torch.ops.inference_performance_lab.fused_add_rms_norm(ex, er, w, 1e-6)
+    hx, hr = Guarded(x.shape, off), Guarded(x.shape, off)
+    gxt, grt = hx.load(oracle.tensor_bits(x)), hr.load(oracle.tensor_bits(r))
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(2):
+                torch.ops.inference_performance_lab.fused_add_rms_norm(gxt, grt, w, 1e-6)
+    gxt.copy_(x)
+    grt.copy_(r)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(gxt, ex) and torch.equal(grt, er)
+    for g in (gx, gr, hx, hr):
+        g.assert_guards_intact()
+    del graph
