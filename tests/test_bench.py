@@ -56,3 +56,26 @@ def test_our_arm_fails_loudly_without_a_gpu() -> None:
     out = run_bench("--steps", "2", "--warmup", "3")
     assert out.returncode != 0 and out.stdout.strip() == ""
     assert "needs a CUDA device" in out.stderr
+
+
+@pytest.mark.gpu
+def test_our_arm_prints_the_full_contract_line_on_a_gpu() -> None:
+    """Our arm on a B200: one JSON line with the roofline, CPU-baseline, end-to-end, launch-count and
+    clock keys, the roofline fraction computed from the measured peak, inputs larger than L2."""
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test run without a CUDA device")
+    out = run_bench("--steps", "20", "--warmup", "3", "--e2e-steps", "5", "--cpu-seconds", "0.5")
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [line for line in out.stdout.splitlines() if line.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["metric"] == "add+RMSNorm achieved HBM GB/s" and d["n_gpus"] == 1 and d["steps"] == 20
+    assert d["dtype"] == "bf16" and d["config"]["kernel"].startswith("rmsnorm_") and "l2" in d["config"]
+    rl = d["roofline"]
+    assert rl["bound"] == "hbm" and rl["unit"] == "GB/s" and rl["peak"] > 0
+    assert abs(rl["frac"] - rl["achieved"] / rl["peak"]) < 1e-9 and 0.3 < rl["frac"] < 1.2
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] > 0
+    e2e = d["e2e"]
+    assert e2e["h2d_bytes_per_step"] == e2e["d2h_bytes_per_step"] == 2048 * 3584 * 2 * 2 and e2e["value"] > 0
+    assert d["gpu_launches"] == 20
+    assert {"sm_mhz", "sm_max_mhz", "reasons"} <= set(d["clocks"])
