@@ -67,3 +67,20 @@ def test_fp8_plans_respect_kernel_preconditions(rows, hidden, x_off, r_off, out8
                                                          BASE + (1 << 34) + 2 * r_off, BASE + (1 << 35), rows, hidden)
     # The fp8 op's vector kernels need x and residual 16-byte aligned and an 8-byte aligned output.
     check(name, rows, hidden, x_off, r_off, 0, "fp8", out8_off)
+
+
+@settings(max_examples=400, deadline=None)
+@given(rows=st.integers(min_value=0, max_value=20000), inter=st.integers(min_value=0, max_value=60000),
+       out_off=st.integers(min_value=0, max_value=31), in_off=st.integers(min_value=0, max_value=31))
+def test_silu_plans_take_the_widest_vector_their_alignment_allows(rows, inter, out_off, in_off) -> None:
+    name = capi.silu_and_mul_plan(BASE + 2 * out_off, BASE + (1 << 34) + 2 * in_off, rows, inter)
+    if rows * inter == 0:
+        assert name == "none"
+        return
+    offset_bytes = (2 * out_off) | (2 * in_off)
+    if inter % 16 == 0 and offset_bytes % 32 == 0:
+        assert name == "silu_vector_kernel<32>", name  # 32-byte packs: gate, up and out rows all aligned
+    elif inter % 8 == 0 and offset_bytes % 16 == 0:
+        assert name == "silu_vector_kernel<16>", name
+    else:
+        assert name == "silu_scalar_kernel", name
