@@ -64,7 +64,7 @@ IPL_API ipl_status ipl_fused_add_rms_norm_bf16(void* x, void* residual, const vo
  *   output = bf16((fp32(input) * rsqrt(mean(fp32(input)^2) + epsilon)) * fp32(weight))
  *
  * input, output: [rows, hidden_size] contiguous; weight: [hidden_size]. Any alignment is
- * accepted (output sharing input's offset modulo 16 bytes takes the staged kernel).
+ * accepted (output sharing input's offset modulo 16 bytes keeps the vectorised kernels).
  *
  * No counterpart in the reference's C++ sources: it is the plain rms_norm of the vLLM IR that
  * the reference's plugin targets (vllm/ir/ops/layernorm.py:9-21 of vLLM 0.22, the op before the
