@@ -97,13 +97,11 @@ struct RmsPlan {
 
 // Kernel names as reported by the plan queries (static strings).
 const char* rms_kernel_name(const RmsPlan& plan, int mode) {
-    static const char* const kStagedNames[3][5] = {
+    static const char* const kStagedNames[2][5] = {  // bf16 outputs only
         {"rmsnorm_staged_kernel<1>", "rmsnorm_staged_kernel<2>", "rmsnorm_staged_kernel<4>",
          "rmsnorm_staged_kernel<8>", "rmsnorm_staged_kernel<16>"},
         {"rmsnorm_staged_kernel<1, plain>", "rmsnorm_staged_kernel<2, plain>", "rmsnorm_staged_kernel<4, plain>",
-         "rmsnorm_staged_kernel<8, plain>", "rmsnorm_staged_kernel<16, plain>"},
-        {"rmsnorm_staged_kernel<1, fp8>", "rmsnorm_staged_kernel<2, fp8>", "rmsnorm_staged_kernel<4, fp8>",
-         "rmsnorm_staged_kernel<8, fp8>", "rmsnorm_staged_kernel<16, fp8>"}};
+         "rmsnorm_staged_kernel<8, plain>", "rmsnorm_staged_kernel<16, plain>"}};
     static const char* const kWarpNames[3][3] = {
         {"rmsnorm_warp_kernel<1>", "rmsnorm_warp_kernel<2>", "rmsnorm_warp_kernel<4>"},
         {"rmsnorm_warp_kernel<1, plain>", "rmsnorm_warp_kernel<2, plain>", "rmsnorm_warp_kernel<4, plain>"},
@@ -125,7 +123,7 @@ const char* rms_kernel_name(const RmsPlan& plan, int mode) {
         case RmsFamily::kNone: return "none";
         case RmsFamily::kStaged:
             while ((1 << i) < plan.warps_per_row) ++i;
-            return kStagedNames[mode][i];
+            return mode == kModeFusedFp8 ? "invalid" : kStagedNames[mode][i];
         case RmsFamily::kWarpRow:
             while ((1 << i) < plan.chunks_per_lane) ++i;
             return kWarpNames[mode][i];
