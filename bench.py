@@ -1,11 +1,13 @@
 """Benchmark of the fused add+RMSNorm hot path (and SiLU-and-mul) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload rmsnorm|rmsnorm-misaligned|silu|rmsnorm-sharded]
+                    [--workload rmsnorm|rmsnorm-misaligned|silu|rmsnorm-sharded|rmsnorm-plain|rmsnorm-fp8]
+                    [--no-subrecords]
 
-Prints ONE JSON line on rank 0. Under torchrun (N > 1) every rank runs its own GPU; the timed
-region is bracketed by a barrier and a device synchronise on both sides, and the elapsed time is
-the max over ranks.
+Prints ONE JSON line on rank 0. Under torchrun (N > 1) every rank runs its own GPU; each timed
+region is bracketed by a device synchronise and a barrier on both sides, and the elapsed time is
+the max over ranks. The ranks' control plane (barriers, max over ranks, the parity verdicts) is a
+gloo process group on the host: no NCCL, and no collective on the data path.
 
 A step is one call of the op on one batch already resident in HBM:
 
@@ -18,15 +20,28 @@ A step is one call of the op on one batch already resident in HBM:
 * ``rmsnorm-sharded``: bf16 [262144, 8192], eps 1e-5, rows split across the ranks with no
   collective (strong scaling); each rank generates its shard on its own device from seed + rank.
 
+Unless ``--no-subrecords``, the line for the default workload also carries ``sharded``,
+``misaligned`` and ``silu`` records: the other three workloads measured the same way in the same
+run, each with its kernel, timings, roofline fraction and an oracle check of its outputs.
+
+Timing: W warm-up steps, then the K steps are enqueued while the device is held by a short sleep
+kernel placed before the start event (NVBench's blocking-kernel method), so the timed region is
+the device running the K launches back to back, not the host's pace of enqueuing them. The host's
+cost per call, whether all K launches were queued before the region started, the same K steps
+launched just in time (no hold) and a CUDA-graph replay of them are reported beside it.
+
 Metric: algorithmic HBM bytes per step (add+RMSNorm: 4*H*2 per row = read x, r + write x, r;
 weight excluded; SiLU: 6 per output element) over the device time, in GB/s, summed over ranks.
-``roofline`` relates the kernel's per-launch time to the measured HBM copy peak;
+``roofline`` relates the kernel's per-launch time to the measured HBM copy peak and carries the
+DRAM traffic per launch measured by ncu (profiles/dram_traffic_per_launch.json);
 ``cpu_baseline`` is the reference's CPU path (its torch fp32 oracle restated, oracle/oracle.py)
 timed on this host; ``e2e`` repeats the metric through the public op with the inputs copied from
 pinned host memory and the results copied back inside the timed region.
 
 ``--impl reference`` times the reference's CPU path alone (rank 0; other ranks exit) on the same
-workload and prints the same metric.
+workload and prints the same metric. When the reference's own CUDA kernels have been built for
+sm_100a (oracle/build_ref_kernels.py) and a GPU is present, its line also carries
+``reference_cuda_kernels``: those kernels timed the same way on the same workloads, on this box.
 """
 
 from __future__ import annotations
@@ -48,6 +63,9 @@ L2_BYTES = 126 * 1024 * 1024
 MEASURED_PEAKS = REPO_ROOT / "MEASURED_PEAKS.json"
 TRAFFIC_FILE = REPO_ROOT / "profiles" / "dram_traffic_per_launch.json"
 FALLBACK_HBM_GBS = 6650.0
+# Device clock used to size the hold (cycles of torch.cuda._sleep): at or above the B200's
+# 1965 MHz maximum, so that the hold lasts at least as long as asked.
+HOLD_CLOCK_GHZ = 2.0
 
 WORKLOADS = {
     "rmsnorm": {"op": "fused_add_rms_norm", "rows": 2048, "hidden": 3584, "eps": 1e-6, "offset": 0},
@@ -59,9 +77,15 @@ WORKLOADS = {
     "rmsnorm-fp8": {"op": "fused_add_rms_norm_static_fp8_quant", "rows": 2048, "hidden": 3584, "eps": 1e-6,
                     "offset": 0},
 }
+# Records added to the default workload's line: name -> workload.
+SUBRECORDS = {"sharded": "rmsnorm-sharded", "misaligned": "rmsnorm-misaligned", "silu": "silu"}
+# Rows of a batch checked against the oracle: every row up to this many, else a sample of at least
+# 64 rows that includes the first and the last.
+CHECK_ALL_ROWS = 4096
+CHECK_SAMPLE_ROWS = 64
 
 
-def workload_name(args, spec) -> str:
+def workload_name(spec) -> str:
     if spec["op"] == "rms_norm":
         return f"rms_norm bf16 [{spec['rows']}, {spec['hidden']}] eps {spec['eps']:g} (out of place)"
     if spec["op"] == "fused_add_rms_norm_static_fp8_quant":
@@ -97,11 +121,16 @@ def load_peak() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def load_traffic(key: str):
+def load_traffic(workload: str) -> dict | None:
+    """ncu's DRAM bytes per launch of this workload's kernel (steady state: the mean over
+    back-to-back launches after the first, each launch's write-back of its predecessor's
+    outputs included), with the command that measured it."""
     try:
-        return json.loads(TRAFFIC_FILE.read_text()).get(key)
+        table = json.loads(TRAFFIC_FILE.read_text())
     except (OSError, ValueError):
         return None
+    entry = table.get("workloads", {}).get(workload)
+    return entry if isinstance(entry, dict) else None
 
 
 # ------------------------------------------------------------------------------------------
@@ -161,6 +190,7 @@ class ClockSampler:
             time.sleep(0.002)
 
     def __enter__(self):
+        self._stop.clear()
         if self._nvml is not None:
             self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
@@ -170,6 +200,7 @@ class ClockSampler:
         self._stop.set()
         if self._thread is not None:
             self._thread.join()
+            self._thread = None
             try:
                 self._sample()  # one sample after the region ends, so that short regions have one
             except Exception:
@@ -187,58 +218,72 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------
-# distributed plumbing (barrier + max over ranks only; the data path has no collective)
+# distributed plumbing: a gloo group on the host (barriers, max over ranks, verdicts)
 
 
 class Dist:
-    def __init__(self, use_gpu: bool, timeout_s: float = 300.0) -> None:
+    def __init__(self, timeout_s: float = 300.0, single: bool = False) -> None:
         # The timeout bounds every collective: a rank that failed or left ends the others' next
         # barrier with an error instead of a hang (300 s covers a fresh box's first torch import).
-        self.world = int(os.environ.get("WORLD_SIZE", "1"))
-        self.rank = int(os.environ.get("RANK", "0"))
-        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.world = 1 if single else int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = 0 if single else int(os.environ.get("RANK", "0"))
+        self.local_rank = 0 if single else int(os.environ.get("LOCAL_RANK", "0"))
         self.pg = None
         if self.world > 1:
             import datetime
 
             import torch.distributed as dist
 
-            backend = "nccl" if use_gpu else "gloo"
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=timeout_s))
             self.pg = dist
 
     def barrier(self) -> None:
         if self.pg is not None:
-            import torch
-
-            self.pg.barrier(device_ids=[self.local_rank] if torch.cuda.is_available() else None)
+            self.pg.barrier()
 
     def max(self, value: float) -> float:
         if self.pg is None:
             return value
         import torch
 
-        t = torch.tensor([value], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+        t = torch.tensor([value], dtype=torch.float64)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
+
+    def all(self, flag: bool) -> bool:
+        if self.pg is None:
+            return bool(flag)
+        import torch
+
+        t = torch.tensor([1 if flag else 0], dtype=torch.int64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MIN)
+        return bool(t.item())
+
+    def gather(self, value) -> list:
+        if self.pg is None:
+            return [value]
+        out = [None] * self.world
+        self.pg.all_gather_object(out, value)
+        return out
 
     def close(self) -> None:
         if self.pg is not None:
             self.pg.destroy_process_group()
 
 
-
 # ------------------------------------------------------------------------------------------
-# per-op workload: inputs, the call, the CPU reference call, host buffers for the e2e leg
+# per-op workload: inputs, the call, the oracle check, host buffers for the e2e leg
 
 
 class OpWorkload:
-    """Everything op-specific: device batches, the op call, its kernel plan, the reference's CPU
-    call on a sample, and which tensors an end-to-end step uploads and downloads."""
+    """Everything op-specific: device batches, the op call, its kernel plan, the check of one call
+    against the oracle, the reference's CPU call on a sample, and which tensors an end-to-end step
+    uploads and downloads."""
 
-    def __init__(self, spec) -> None:
+    def __init__(self, spec, namespace: str = "inference_performance_lab") -> None:
         self.spec = spec
         self.op = spec["op"]
+        self.namespace = namespace
 
     def make_sets(self, rows: int, seed: int, device, sets: int):
         """`sets` batches (dicts of device tensors) and the tensors they share (weight, scale)."""
@@ -281,19 +326,18 @@ class OpWorkload:
 
         import torch
 
-        ops = torch.ops.inference_performance_lab
+        ops = getattr(torch.ops, self.namespace)
         eps = self.spec.get("eps")
         if self.op == "silu_and_mul":
-            return functools.partial(ops.silu_and_mul.default, batch["out"], batch["x"])
+            # The reference's own library has the vectorised kernel under the packed op name only.
+            name = "silu_and_mul_packed" if self.namespace != "inference_performance_lab" else "silu_and_mul"
+            return functools.partial(getattr(ops, name).default, batch["out"], batch["x"])
         if self.op == "rms_norm":
             return functools.partial(ops.rms_norm.default, batch["out"], batch["x"], shared["w"], eps)
         if self.op == "fused_add_rms_norm_static_fp8_quant":
             return functools.partial(ops.fused_add_rms_norm_static_fp8_quant.default, batch["out"], batch["x"],
                                      batch["r"], shared["w"], shared["scale"], eps)
         return functools.partial(ops.fused_add_rms_norm.default, batch["x"], batch["r"], shared["w"], eps)
-
-    def call(self, batch, shared) -> None:
-        self.bind(batch, shared)()
 
     def plan(self, batch, shared, rows: int) -> str:
         from inference_performance_lab.kernels import capi
@@ -308,6 +352,68 @@ class OpWorkload:
             return capi.fused_add_rms_norm_static_fp8_quant_plan(
                 batch["out"].data_ptr(), batch["x"].data_ptr(), batch["r"].data_ptr(), w, rows, hidden)
         return capi.fused_add_rms_norm_plan(batch["x"].data_ptr(), batch["r"].data_ptr(), w, rows, hidden)
+
+    def check(self, batch, shared, rows: int) -> dict:
+        """One op call on `batch` (fresh inputs), with its rows compared against the C oracle: every
+        row up to CHECK_ALL_ROWS rows, else CHECK_SAMPLE_ROWS spread over the batch including the
+        first and last. Residuals must match bit for bit; bf16 outputs must be within rtol = atol =
+        1e-2 and one bf16 ulp of the oracle; e4m3 outputs within one e4m3 step. Outside every timed
+        region: the oracle is the checker here, never the thing measured."""
+        import numpy as np
+        import torch
+
+        from oracle import oracle
+
+        if rows <= CHECK_ALL_ROWS:
+            index = list(range(rows))
+        else:
+            step = (rows - 1) / (CHECK_SAMPLE_ROWS - 1)
+            index = sorted({round(i * step) for i in range(CHECK_SAMPLE_ROWS)} | {0, rows - 1})
+        idx = torch.tensor(index, dtype=torch.int64, device=batch["x"].device)
+
+        def take(t):
+            return t.index_select(0, idx).contiguous()
+
+        before = {k: take(v) for k, v in batch.items() if k in ("x", "r")}
+        self.bind(batch, shared)()
+        torch.cuda.synchronize()
+        result = {"rows_checked": len(index), "residual_exact": None, "max_ulp": None, "max_abs_err": None}
+
+        def compare_bf16(got_t, want_bits) -> bool:
+            got = oracle.tensor_bits(got_t)
+            g, w = oracle.bf16_bits_to_f32(got), oracle.bf16_bits_to_f32(want_bits)
+            finite = np.isfinite(w)
+            err = np.abs(g - w)
+            result["max_abs_err"] = float(err[finite].max(initial=0.0))
+            ordered = [np.where(a.astype(np.int32) & 0x8000, 0x8000 - a.astype(np.int32), a.astype(np.int32))
+                       for a in (got, want_bits)]
+            result["max_ulp"] = int(np.abs(ordered[0] - ordered[1]).max(initial=0))
+            close = np.all((err <= 1e-2 + 1e-2 * np.abs(w)) | ~finite) and np.array_equal(np.isnan(g), np.isnan(w))
+            return bool(close) and result["max_ulp"] <= 1
+
+        if self.op == "silu_and_mul":
+            want = oracle.c_silu_and_mul(oracle.tensor_bits(before["x"]))
+            ok = compare_bf16(take(batch["out"]), want)
+        elif self.op == "rms_norm":
+            want = oracle.c_rms_norm(oracle.tensor_bits(before["x"]), oracle.tensor_bits(shared["w"]), self.spec["eps"])
+            ok = compare_bf16(take(batch["out"]), want)
+        elif self.op == "fused_add_rms_norm_static_fp8_quant":
+            want8, want_res = oracle.c_fused_add_rms_norm_static_fp8_quant(
+                oracle.tensor_bits(before["x"]), oracle.tensor_bits(before["r"]), oracle.tensor_bits(shared["w"]),
+                float(shared["scale"].item()), self.spec["eps"])
+            result["residual_exact"] = bool(np.array_equal(oracle.tensor_bits(take(batch["r"])), want_res))
+            got8 = take(batch["out"]).view(torch.uint8).cpu().numpy().astype(np.int32)
+            ordered = [np.where(a & 0x80, 0x80 - a, a) for a in (got8, want8.astype(np.int32))]
+            result["max_ulp"] = int(np.abs(ordered[0] - ordered[1]).max(initial=0))
+            ok = result["residual_exact"] and result["max_ulp"] <= 1
+        else:
+            want_out, want_res = oracle.c_fused_add_rms_norm(
+                oracle.tensor_bits(before["x"]), oracle.tensor_bits(before["r"]), oracle.tensor_bits(shared["w"]),
+                self.spec["eps"])
+            result["residual_exact"] = bool(np.array_equal(oracle.tensor_bits(take(batch["r"])), want_res))
+            ok = compare_bf16(take(batch["x"]), want_out) and result["residual_exact"]
+        result["parity_ok"] = bool(ok)
+        return result
 
     def e2e_inputs(self, batch):
         """Device tensors an end-to-end step fills from pinned host memory."""
@@ -362,6 +468,169 @@ class OpWorkload:
 
 
 # ------------------------------------------------------------------------------------------
+# device timing
+
+
+def time_calls(calls, steps: int, warmup: int, stream, dist, clocks: ClockSampler | None) -> dict:
+    """W warm-up calls, then K calls timed on the device.
+
+    The K launches are enqueued while the device sleeps in a hold kernel issued before the start
+    event, so the events bracket the device running them back to back (the host's enqueue pace is
+    reported separately as ``host_us_per_call``). ``queued_before_start`` says whether every launch
+    was in the queue before the start event fired. The same K calls are then run again without
+    the hold, as a caller that launches just in time would: ``unqueued_us_per_step``, and
+    ``idle_us_per_step``, the device time per step that the host's pace adds."""
+    import torch
+
+    n = len(calls)
+    t0 = time.perf_counter()
+    for i in range(warmup):
+        calls[i % n]()
+    host_warm = (time.perf_counter() - t0) / max(warmup, 1)
+    order = [calls[(warmup + i) % n] for i in range(steps)]
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    hold_s = min(max(50e-6, 2.0 * steps * host_warm + 20e-6), 0.2)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if clocks is not None:
+        clocks.__enter__()
+    try:
+        torch.cuda._sleep(int(hold_s * HOLD_CLOCK_GHZ * 1e9))
+        start.record(stream)
+        h0 = time.perf_counter()
+        for call in order:
+            call()
+        host_s = time.perf_counter() - h0
+        queued = not start.query()
+        end.record(stream)
+        end.synchronize()
+    finally:
+        if clocks is not None:
+            clocks.__exit__(None, None, None)
+    torch.cuda.synchronize()
+    dist.barrier()
+    local_ms = start.elapsed_time(end)
+    elapsed_ms = dist.max(local_ms)
+
+    # Just in time: the same calls with no hold (the host's pace included).
+    torch.cuda.synchronize()
+    u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    u0.record(stream)
+    for call in order:
+        call()
+    u1.record(stream)
+    u1.synchronize()
+    unqueued_ms = u0.elapsed_time(u1)
+    return {
+        "local_ms": local_ms,
+        "elapsed_ms": elapsed_ms,
+        "us_per_step": elapsed_ms / steps * 1e3,
+        "host_us_per_call": host_s / steps * 1e6,
+        "queued_before_start": bool(queued),
+        "hold_us": hold_s * 1e6,
+        "unqueued_us_per_step": unqueued_ms / steps * 1e3,
+        "idle_us_per_step": max(0.0, (unqueued_ms - local_ms) / steps * 1e3),
+    }
+
+
+def graph_replay_us(calls, steps: int, stream) -> float:
+    """Per-launch device time of the same launches replayed from a CUDA graph (launch cost gone)."""
+    import torch
+
+    sets = len(calls)
+    graph_steps = min(max(steps, sets), 100 * sets)
+    graph_steps -= graph_steps % sets
+    graph_steps = max(graph_steps, sets)
+    graph = torch.cuda.CUDAGraph()
+    capture_stream = torch.cuda.Stream()
+    capture_stream.wait_stream(stream)
+    with torch.cuda.stream(capture_stream):
+        with torch.cuda.graph(graph, stream=capture_stream):
+            for i in range(graph_steps):
+                calls[i % sets]()
+    stream.wait_stream(capture_stream)
+    graph.replay()
+    torch.cuda.synchronize()
+    replays = max(1, steps // graph_steps)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(replays):
+        graph.replay()
+    g1.record(stream)
+    g1.synchronize()
+    us = g0.elapsed_time(g1) / (replays * graph_steps) * 1e3
+    del graph
+    return us
+
+
+def rotation_sets(per_step: int) -> int:
+    """Batches to rotate over so that each step's inputs are cold in L2 (>= 4x L2 in total)."""
+    return max(1, math.ceil(4 * L2_BYTES / per_step)) if per_step < 4 * L2_BYTES else 1
+
+
+def measure_workload(name: str, spec, dist, device, stream, steps: int, warmup: int, *, graph: bool,
+                     namespace: str = "inference_performance_lab", with_plan: bool = True) -> dict:
+    """Inputs for this rank, one checked call, then the timing of K steps (see time_calls)."""
+    import torch
+
+    from inference_performance_lab.kernels.sharding import row_shard, shard_seed
+
+    workload = OpWorkload(spec, namespace)
+    if spec.get("sharded"):
+        shard = row_shard(spec["rows"], dist.world, dist.rank)
+        rows, total_rows = shard.rows, spec["rows"]
+    else:
+        rows, total_rows = spec["rows"], spec["rows"] * dist.world
+    per_step = step_bytes(spec, rows)
+    sets = rotation_sets(per_step)
+    batches, shared = workload.make_sets(rows, shard_seed(0, dist.rank), device, sets)
+    parity = workload.check(batches[0], shared, rows)
+    calls = [workload.bind(batch, shared) for batch in batches]
+    clocks = ClockSampler(dist.local_rank)
+    timing = time_calls(calls, steps, warmup, stream, dist, clocks)
+    graph_us = graph_replay_us(calls, steps, stream) if graph else None
+    kernel = workload.plan(batches[0], shared, rows) if with_plan else None
+    peak, peak_kind = load_peak()
+    local_us = timing["local_ms"] / steps * 1e3
+    total_bytes = step_bytes(spec, total_rows)
+    result = {
+        "workload": workload_name(spec),
+        "metric": workload.metric(),
+        "rows_per_rank": rows,
+        "bytes_per_step_per_rank": per_step,
+        "l2": (f"inputs rotate over {sets} batches ({sets * per_step / 1e6:.0f} MB per rank, > 4x the 126 MB L2)"
+               if sets > 1 else "inputs larger than the 126 MB L2"),
+        "kernel": kernel,
+        "steps": steps,
+        "warmup": warmup,
+        "value": total_bytes / (timing["us_per_step"] * 1e-6) / 1e9,
+        "unit": "GB/s",
+        "rows_per_s": total_rows / (timing["us_per_step"] * 1e-6),
+        "us_per_step": timing["us_per_step"],
+        "roofline_frac": per_step / (local_us * 1e-6) / 1e9 / peak,
+        "graph_replay_us_per_launch": graph_us,
+        "graph_replay_frac": (per_step / (graph_us * 1e-6) / 1e9 / peak) if graph_us else None,
+        "launch": {k: timing[k] for k in ("host_us_per_call", "queued_before_start", "hold_us",
+                                          "unqueued_us_per_step", "idle_us_per_step")},
+        "parity": parity,
+        "clocks": clocks.summary(),
+        "_local_us": local_us,
+        "_peak": (peak, peak_kind),
+        "_calls": calls,
+        "_batches": batches,
+        "_shared": shared,
+        "_workload": workload,
+        "_rows": rows,
+    }
+    return result
+
+
+def public(record: dict) -> dict:
+    return {k: v for k, v in record.items() if not k.startswith("_")}
+
+
+# ------------------------------------------------------------------------------------------
 # CPU path of the reference (the oracle's torch restatement of reference.py)
 
 
@@ -390,6 +659,51 @@ def cpu_reference_rate(spec, seconds: float, sample_rows: int | None = None) -> 
                   f"({median * 1e3:.2f} ms/call, {rows / median:.0f} rows/s), torch fp32 on CPU",
         "ms_per_call": median * 1e3,
         "rows_per_s": rows / median,
+    }
+
+
+def reference_cuda_kernels(args) -> dict | None:
+    """The reference's own CUDA kernels, built for sm_100a from its sources (oracle/_ref), timed on
+    this GPU exactly as our arm times ours, on the same workloads, each checked against the oracle.
+    None when the library is absent or there is no GPU."""
+    import torch
+
+    from oracle import build_ref_kernels
+
+    if not torch.cuda.is_available():
+        return None
+    if not build_ref_kernels.load():
+        return {"unavailable": "oracle/_ref/libref_kernels.so not built (oracle/build_ref_kernels.py)"}
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream()
+    dist = Dist(single=True)
+    records = {}
+    kernels = {
+        "rmsnorm": "fused_add_rms_norm_bf16_packed_cached_kernel<3584>",
+        "misaligned": "fused_add_rms_norm_bf16_cached_kernel<3584>",
+        "silu": "silu_and_mul_bf16_packed_kernel (op silu_and_mul_packed)",
+        "sharded": "fused_add_rms_norm_bf16_generic_kernel",
+    }
+    names = {"rmsnorm": "rmsnorm", **SUBRECORDS}
+    with torch.inference_mode():
+        for key, workload in names.items():
+            spec = dict(WORKLOADS[workload])
+            if spec.get("sharded"):
+                steps, warmup = min(args.steps, 40), max(3, min(args.warmup, 5))
+            else:
+                steps, warmup = min(args.steps, 1000), args.warmup
+            rec = measure_workload(workload, spec, dist, device, stream, steps, warmup,
+                                   graph=not spec.get("sharded"), namespace="inference_performance_lab_ref",
+                                   with_plan=False)
+            rec["kernel"] = kernels[key]
+            records[key] = public(rec)
+            del rec
+            torch.cuda.empty_cache()
+    return {
+        "what": "the reference's csrc kernels compiled for sm_100a from its unmodified sources "
+                "(oracle/build_ref_kernels.py), run through its own op wrappers on this GPU, timed as our arm",
+        **records,
     }
 
 
@@ -430,11 +744,18 @@ def run_reference(args, spec) -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": workload_name(args, spec), "rows_per_step": rows},
+        "config": {"workload": workload_name(spec), "rows_per_step": rows},
         "rows_per_s": rows * args.steps / elapsed,
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if args.workload == "rmsnorm" and not args.no_subrecords:
+        try:
+            kernels = reference_cuda_kernels(args)
+        except Exception as exc:  # the CPU arm's line stands on its own
+            kernels = {"unavailable": f"{type(exc).__name__}: {exc}"}
+        if kernels is not None:
+            line["reference_cuda_kernels"] = kernels
     print(json.dumps(line), flush=True)
 
 
@@ -446,145 +767,121 @@ def run_ours(args, spec) -> None:
     import torch
 
     from inference_performance_lab.kernels import capi, extension
-    from inference_performance_lab.kernels.sharding import row_shard, shard_seed
 
     if not torch.cuda.is_available():
         raise SystemExit("bench.py needs a CUDA device (there is no CPU fallback)")
-    dist = Dist(use_gpu=True)
+    dist = Dist()
     torch.cuda.set_device(dist.local_rank)
     device = torch.device("cuda", dist.local_rank)
     extension.load_extension()
     stream = torch.cuda.current_stream()
 
-    workload = OpWorkload(spec)
-    if spec.get("sharded"):
-        rows = row_shard(spec["rows"], dist.world, dist.rank).rows
-        scaling = "strong"
-    else:
-        rows = spec["rows"]
-        scaling = "weak"
-    per_step = step_bytes(spec, rows)
-    sets = max(1, math.ceil(4 * L2_BYTES / per_step)) if per_step < 4 * L2_BYTES else 1
-    batches, shared = workload.make_sets(rows, shard_seed(0, dist.rank), device, sets)
-    calls = [workload.bind(batch, shared) for batch in batches]
-
-    def step(i: int) -> None:
-        calls[i % sets]()
-
     with torch.inference_mode():
-        for i in range(args.warmup):
-            step(i)
-        torch.cuda.synchronize()
-        dist.barrier()
-        torch.cuda.synchronize()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        order = [calls[(args.warmup + i) % sets] for i in range(args.steps)]
-        with ClockSampler(dist.local_rank) as clocks:
-            start.record(stream)
-            for call in order:
-                call()
-            end.record(stream)
-            end.synchronize()
-        torch.cuda.synchronize()
-        dist.barrier()
-        local_ms = start.elapsed_time(end)
-        elapsed_ms = dist.max(local_ms)
-
-        # The same steps replayed from a CUDA graph (launch overhead removed): kernel time.
-        graph_steps = min(args.steps, 100 * sets)
-        graph_steps -= graph_steps % sets
-        graph_steps = max(graph_steps, sets)
-        graph = torch.cuda.CUDAGraph()
-        capture_stream = torch.cuda.Stream()
-        capture_stream.wait_stream(stream)
-        with torch.cuda.stream(capture_stream):
-            with torch.cuda.graph(graph, stream=capture_stream):
-                for i in range(graph_steps):
-                    step(i)
-        stream.wait_stream(capture_stream)
-        graph.replay()
-        torch.cuda.synchronize()
-        replays = max(1, args.steps // graph_steps)
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        for _ in range(replays):
-            graph.replay()
-        g1.record(stream)
-        g1.synchronize()
-        graph_ms_per_step = g0.elapsed_time(g1) / (replays * graph_steps)
-        del graph
-
-        e2e = run_e2e(args, spec, workload, rows, batches, shared, stream, dist)
+        main = measure_workload(args.workload, spec, dist, device, stream, args.steps, args.warmup, graph=True)
+        workload, rows = main["_workload"], main["_rows"]
+        e2e = run_e2e(args, spec, workload, rows, main["_batches"], main["_shared"], stream, dist)
         same_traffic = copy_same_traffic(workload, rows, device, args.steps)
+        for key in [k for k in main if k.startswith("_") and k not in ("_local_us", "_peak", "_rows")]:
+            del main[key]
+        torch.cuda.empty_cache()
+
+        subrecords = {}
+        if args.workload == "rmsnorm" and not args.no_subrecords:
+            for key, name in SUBRECORDS.items():
+                sub_spec = dict(WORKLOADS[name])
+                if sub_spec.get("sharded"):
+                    steps, warmup = min(args.steps, 40), max(3, min(args.warmup, 5))
+                else:
+                    steps, warmup = min(args.steps, 1000), args.warmup
+                rec = measure_workload(name, sub_spec, dist, device, stream, steps, warmup,
+                                       graph=not sub_spec.get("sharded"))
+                rec["parity"]["parity_ok_all_ranks"] = dist.all(rec["parity"]["parity_ok"])
+                per_rank = dist.gather({"rank": dist.rank, "us_per_step": rec["_local_us"],
+                                        "roofline_frac": rec["roofline_frac"], "rows": rec["rows_per_rank"],
+                                        "parity_ok": rec["parity"]["parity_ok"]})
+                rec["per_rank"] = per_rank
+                traffic = load_traffic(name)
+                rec["traffic"] = traffic
+                subrecords[key] = public(rec)
+                del rec
+                torch.cuda.empty_cache()
 
     # Every bounded wait of the staged kernel must have completed: a nonzero fault word means a
     # kernel gave up and its outputs are incomplete, so the run is not a measurement.
     fault_flags = int(dist.max(float(capi.device_fault_flags(dist.local_rank))))
     if fault_flags:
         raise SystemExit(f"device fault word {fault_flags:#x}: a kernel gave up on a wait")
+    parity_ok = dist.all(main["parity"]["parity_ok"])
 
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         sample_rows = spec["rows"] if not spec.get("sharded") else 1024
         cpu = cpu_reference_rate(spec, args.cpu_seconds, sample_rows=sample_rows)
 
-    ms_per_step = elapsed_ms / args.steps
-    total_bytes = per_step * dist.world if not spec.get("sharded") else step_bytes(spec, spec["rows"])
-    value = total_bytes / (ms_per_step * 1e-3) / 1e9
-    peak, peak_kind = load_peak()
-    achieved = per_step / (local_ms / args.steps * 1e-3) / 1e9
+    peak, peak_kind = main["_peak"]
+    local_us = main["_local_us"]
+    per_step = main["bytes_per_step_per_rank"]
+    achieved = per_step / (local_us * 1e-6) / 1e9
     traffic = load_traffic(args.workload)
+    traffic_bytes = None
     if traffic is not None:
-        traffic = traffic * rows / WORKLOADS[args.workload]["rows"]
-    total_rows = rows * dist.world if not spec.get("sharded") else spec["rows"]
+        traffic_bytes = traffic["bytes_per_launch"] * main["rows_per_rank"] / traffic["rows"]
     line = {
-        "metric": workload.metric(),
-        "value": value,
+        "metric": main["metric"],
+        "value": main["value"],
         "unit": "GB/s",
         "n_gpus": dist.world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": ms_per_step,
+        "ms_per_step": main["us_per_step"] / 1e3,
         "higher_is_better": True,
-        "scaling": scaling,
+        "scaling": "strong" if spec.get("sharded") else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) inputs on device, the reference's recipe)",
         "config": {
-            "workload": workload_name(args, spec),
-            "rows_per_rank": rows,
+            "workload": main["workload"],
+            "rows_per_rank": main["rows_per_rank"],
             "bytes_per_step_per_rank": per_step,
-            "l2": f"inputs rotate over {sets} batches ({sets * per_step / 1e6:.0f} MB per rank, "
-                  f"> 4x the 126 MB L2)" if sets > 1 else "inputs larger than the 126 MB L2",
-            "kernel": workload.plan(batches[0], shared, rows),
+            "l2": main["l2"],
+            "kernel": main["kernel"],
+            "launch": "K launches enqueued behind a device-side hold before the start event: "
+                      "the device runs them back to back",
         },
         "pct_of_peak": 100.0 * achieved / peak,
-        "rows_per_s": total_rows / (ms_per_step * 1e-3),
+        "rows_per_s": main["rows_per_s"],
         # The reference's own microbenchmark counts 10 B per add+RMSNorm element (the weight
         # read for every row as well); the same time at that count, for comparison with it.
-        "gbs_at_reference_byte_count": (value * 10 / 8 if spec["op"] == "fused_add_rms_norm" else value),
+        "gbs_at_reference_byte_count": (main["value"] * 10 / 8 if spec["op"] == "fused_add_rms_norm" else main["value"]),
         "roofline": {
             "bound": "hbm",
             "achieved": achieved,
             "peak": peak,
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": traffic,
+            "traffic": traffic_bytes,
+            "traffic_ratio": (traffic_bytes / per_step) if traffic_bytes else None,
+            "traffic_source": traffic["command"] if traffic else None,
             "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback 6.65 TB/s",
-            "graph_replay_us_per_launch": graph_ms_per_step * 1e3,
-            "graph_replay_achieved": per_step / (graph_ms_per_step * 1e-3) / 1e9,
+            "graph_replay_us_per_launch": main["graph_replay_us_per_launch"],
+            "graph_replay_frac": main["graph_replay_frac"],
             "same_traffic_torch_op": same_traffic,
             "frac_of_same_traffic_torch_op": achieved / same_traffic["achieved"],
         },
+        "launch": main["launch"],
+        "parity": {**main["parity"], "parity_ok_all_ranks": parity_ok},
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": args.steps,
         "fault_flags": fault_flags,
-        "clocks": clocks.summary(),
+        "clocks": main["clocks"],
+        **subrecords,
     }
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
     dist.close()
+    if not parity_ok:
+        raise SystemExit("oracle check of the measured workload failed")
 
 
 def copy_same_traffic(workload, rows: int, device, steps: int) -> dict:
@@ -598,7 +895,7 @@ def copy_same_traffic(workload, rows: int, device, steps: int) -> dict:
     per = 2 * (read_elems + write_elems)
     use_add = read_elems == 2 * write_elems
     n = write_elems if use_add else (read_elems + write_elems) // 2
-    sets = max(1, math.ceil(4 * L2_BYTES / per)) if per < 4 * L2_BYTES else 1
+    sets = rotation_sets(per)
     src = [torch.empty(2 * n if use_add else n, dtype=torch.bfloat16, device=device).normal_() for _ in range(sets)]
     dst = [torch.empty(n, dtype=torch.bfloat16, device=device) for _ in range(sets)]
     if use_add:
@@ -701,9 +998,9 @@ def run_e2e(args, spec, workload, rows: int, batches, shared, stream, dist) -> d
 
 
 def _reserve_stdout_for_the_result() -> None:
-    """Only the result line goes to stdout: libraries that print from C (NCCL's version banner,
-    for one) are sent to stderr by pointing file descriptor 1 there, and Python's stdout is
-    re-opened on a private duplicate of the original descriptor."""
+    """Only the result line goes to stdout: libraries that print from C are sent to stderr by
+    pointing file descriptor 1 there, and Python's stdout is re-opened on a private duplicate of
+    the original descriptor."""
     sys.stdout.flush()
     result_fd = os.dup(1)
     os.dup2(2, 1)
@@ -721,6 +1018,8 @@ def main() -> None:
     parser.add_argument("--e2e-steps", type=int, default=200)
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-subrecords", action="store_true",
+                        help="measure the chosen workload only (no sharded / misaligned / silu records)")
     parser.add_argument("--rows", type=int, default=None,
                         help="override the workload's row count (small cases for profiling)")
     args = parser.parse_args()

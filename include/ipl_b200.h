@@ -141,10 +141,12 @@ IPL_API ipl_status ipl_device_fault_flags(int device, uint32_t* flags);
 IPL_API ipl_status ipl_clear_device_fault_flags(int device);
 
 /*
- * Name of the kernel that ipl_fused_add_rms_norm_bf16 / ipl_rms_norm_bf16 / ipl_silu_and_mul_bf16
- * would launch for
- * these arguments (no launch, no device access). Static string; "none" for an empty batch,
- * "invalid" when the arguments would be rejected.
+ * Name of the kernel that ipl_fused_add_rms_norm_bf16 / ipl_rms_norm_bf16 /
+ * ipl_fused_add_rms_norm_static_fp8_quant / ipl_silu_and_mul_bf16 would launch for these
+ * arguments on the current device (no launch; the device's SM count and shared-memory limit are
+ * read as a call reads them). Where no CUDA device can be queried, a B200's limits are assumed
+ * (148 SMs, 232448 bytes of opt-in shared memory per block). Static string; "none" for an empty
+ * batch, "invalid" when the arguments would be rejected.
  */
 IPL_API const char* ipl_fused_add_rms_norm_plan(const void* x, const void* residual, const void* weight,
                                         int64_t rows, int64_t hidden_size);

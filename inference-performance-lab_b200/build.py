@@ -28,6 +28,9 @@ NATIVE = PACKAGE_ROOT / "inference_performance_lab" / "_native"
 
 LIB_NAME = "libipl_b200.so"
 TORCH_OPS_NAME = "inference_performance_lab_cuda.so"
+# Test-only variant of LIB_NAME (never loaded by the package): see build_wait_test().
+WAIT_TEST_NAME = "test/libipl_b200_waittest.so"
+WAIT_TEST_DEFINES = ["-DIPL_WAIT_LIMIT_NS=1000000ull", "-DIPL_TEST_STAGED_SKIP_ROW=0"]
 
 # Stable ABI target: torch 2.10 (the oldest version that has every call the shim uses).
 TORCH_TARGET_VERSION = "0x020a000000000000"
@@ -122,6 +125,23 @@ def build_native(verbose: bool = False) -> Path:
     return output
 
 
+def build_wait_test(verbose: bool = False) -> Path:
+    """The same kernels and C ABI built for a test of the staged kernel's bounded waits: every wait
+    gives up after 1 ms instead of 2 s, and CTA 0 of the staged kernel never issues its row 0, so
+    the consumers waiting for that row run out of time. A test loads it (ctypes) to check that the
+    kernel then returns, records the fault bit and leaves the context usable."""
+    output = NATIVE / WAIT_TEST_NAME
+    output.parent.mkdir(parents=True, exist_ok=True)
+    sources = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "ipl_b200.h"]
+    flags = [*NVCC_FLAGS, *WAIT_TEST_DEFINES, f"-I{INCLUDE}", f"-I{CSRC}"]
+    stamp = _stamp(sources, flags)
+    if _up_to_date(output, stamp):
+        return output
+    _run([_nvcc(), *flags, "-shared", "-o", str(output), str(CSRC / "ipl_b200.cu")], verbose)
+    _write_stamp(output, stamp)
+    return output
+
+
 def build_torch_ops(verbose: bool = False) -> Path:
     """Compile the stable-ABI op registration, linked against libipl_b200.so."""
     import torch
@@ -162,8 +182,9 @@ def build_torch_ops(verbose: bool = False) -> Path:
     return output
 
 
-def build(verbose: bool = False) -> None:
-    """Build both libraries; concurrent callers (e.g. several ranks) serialise on a lock file."""
+def build(verbose: bool = False, tests: bool = False) -> None:
+    """Build both libraries (and, with ``tests``, the test-only wait-limit variant); concurrent
+    callers (e.g. several ranks) serialise on a lock file."""
     import fcntl
 
     NATIVE.mkdir(parents=True, exist_ok=True)
@@ -172,9 +193,11 @@ def build(verbose: bool = False) -> None:
         try:
             build_native(verbose)
             build_torch_ops(verbose)
+            if tests:
+                build_wait_test(verbose)
         finally:
             fcntl.flock(lock, fcntl.LOCK_UN)
 
 
 if __name__ == "__main__":
-    build(verbose="-q" not in sys.argv)
+    build(verbose="-q" not in sys.argv, tests="--tests" in sys.argv)

@@ -258,7 +258,6 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
         bytes = ((phase + static_cast<uint32_t>(p.hidden) + 7u) >> 3) * 16u;
     };
 
-#ifndef IPL_TUNING_NO_PREFETCH
     // While the previous kernel in the stream drains (this CTA may start before it completes),
     // ask L2 for the rows this CTA copies first, so HBM is busy through the dependency wait. A
     // prefetch only warms L2, the point where every SM's accesses meet, so it cannot return data
@@ -274,7 +273,6 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
             if constexpr (kResidual) bulk_prefetch_l2(reinterpret_cast<const void*>(rbase), bytes);
         }
     }
-#endif
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
@@ -305,15 +303,25 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
             bulk_load(smem_base + layout.weight_raw_offset, reinterpret_cast<const void*>(wbase), wbytes,
                       weight_bar, l2_policy_evict_last());
 
+            // Round of the last copy issued into each stage (-1: none), for the drain below.
+            int last_round[kStagedMaxStages];
+            for (int s = 0; s < p.stages; ++s) last_round[s] = -1;
             const uint64_t policy = l2_policy_evict_first();  // normal and evict_last measured no faster
             for (int j = 0; j < local_rows; ++j) {
                 const int s = j % p.stages;
                 const int round = j / p.stages;
+                // A wait that gives up (or sees a consumer's abort) ends the issuing: nothing
+                // more is copied, and the drain below lets what was issued land.
                 if (round > 0 &&
                     !mbar_wait_bounded(empty_bar + 8u * s, (round - 1) & 1, abort,
                                        kFaultEmptyBarrierTimeout)) {
                     break;
                 }
+#ifdef IPL_TEST_STAGED_SKIP_ROW
+                // Test builds only: CTA 0 never issues this row's copy, so the consumers waiting
+                // for it run out of time (nothing is left in flight for that stage).
+                if (blockIdx.x == 0 && j == IPL_TEST_STAGED_SKIP_ROW) continue;
+#endif
                 uintptr_t xbase, rbase;
                 uint32_t bytes;
                 row_span(row_begin + j, xbase, rbase, bytes);
@@ -324,18 +332,37 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
                 if constexpr (kResidual) {
                     bulk_load(stage + half, reinterpret_cast<const void*>(rbase), bytes, bar, policy);
                 }
+                last_round[s] = round;
             }
+            // Drain: the CTA must not end while a bulk copy still writes its shared memory. Each
+            // stage's full barrier completes one phase per copy, and no copy follows the last one
+            // issued into it, so the phase of that round completes exactly when it has landed
+            // (at once if a consumer already saw it). Bounded by time alone: the abort flag does
+            // not end these waits.
+            for (int s = 0; s < p.stages; ++s) {
+                if (last_round[s] >= 0) {
+                    mbar_wait_timed(full_bar + 8u * static_cast<uint32_t>(s), last_round[s] & 1,
+                                    kFaultCopyDrainTimeout);
+                }
+            }
+            mbar_wait_timed(weight_bar, 0, kFaultCopyDrainTimeout);
         }
         return;
     }
 
     // ---------------- consumers ----------------
+    // Agreed exit: a consumer warp whose bounded wait gives up (it then sets the CTA's abort flag)
+    // or that finds the flag set never leaves early. It keeps its place in every named barrier
+    // below - barrier 1 once, its group's barrier once per row, exactly as many times as its
+    // group partners - and skips only the waits, loads, stores and releases it would have made,
+    // so no warp of the CTA is left waiting at a barrier. `aborted` is made warp-uniform
+    // (__any_sync) after every wait, so each barrier is reached by whole, converged warps.
     const int span = p.chunks_max * 8;
-    if (!mbar_wait_bounded(weight_bar, 0, abort, kFaultFullBarrierTimeout)) return;
+    bool aborted = __any_sync(0xffffffffu, !mbar_wait_bounded(weight_bar, 0, abort, kFaultFullBarrierTimeout));
     // Widen gamma to fp32 once per CTA, aligned to row 0's phase: column c of a row whose
     // phase is row_phase sits at index c + row_phase, so chunk k of such a row lines up with
     // bytes [32k, 32k + 32) of the fp32 copy. Entries outside [0, H) are zero.
-    {
+    if (!aborted) {
         const uint16_t* raw = reinterpret_cast<const uint16_t*>(smem + layout.weight_raw_offset);
         unsigned char* wf = smem + layout.weight_f32_offset;
         for (int i = threadIdx.x; i < span; i += kConsumerThreads) {
@@ -343,8 +370,8 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
             *reinterpret_cast<float*>(wf + gamma_offset(i, half)) =
                 (column >= 0 && column < p.hidden) ? bf16_bits_to_float(raw[column + weight_phase]) : 0.0f;
         }
-        named_barrier_sync(1, kConsumerThreads);
     }
+    named_barrier_sync(1, kConsumerThreads);
     grid_launch_dependents();
     const uint32_t wf_base = smem_base + layout.weight_f32_offset;
 
@@ -369,12 +396,13 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
         // from load order: once all W warps of its group released row j - S, it was loaded.
         const int s = j % p.stages;
         const int round = j / p.stages;
-        if (round > 0 && !spin_until_at_least(released + s, round * kWarpsPerRow, abort,
-                                              kFaultFullBarrierTimeout)) {
-            break;
+        if (!aborted && round > 0) {
+            aborted = !spin_until_at_least(released + s, round * kWarpsPerRow, abort, kFaultFullBarrierTimeout);
         }
+        aborted = __any_sync(0xffffffffu, aborted);
         const uint32_t bar = full_bar + 8u * static_cast<uint32_t>(s);
-        if (!mbar_wait_bounded(bar, round & 1, abort, kFaultFullBarrierTimeout)) break;
+        if (!aborted) aborted = !mbar_wait_bounded(bar, round & 1, abort, kFaultFullBarrierTimeout);
+        aborted = __any_sync(0xffffffffu, aborted);
         const int64_t row = row_begin + j;
         const uintptr_t xa = reinterpret_cast<uintptr_t>(p.x + row * p.hidden);
         const uintptr_t ra = kResidual ? reinterpret_cast<uintptr_t>(p.residual + row * p.hidden) : 0;
@@ -382,7 +410,7 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
         uint16_t* obase = reinterpret_cast<uint16_t*>(oa & ~static_cast<uintptr_t>(15));
         uint16_t* rbase = reinterpret_cast<uint16_t*>(ra & ~static_cast<uintptr_t>(15));
         const int phase = static_cast<int>((xa & 15u) >> 1);
-        const int chunks = (phase + p.hidden + 7) >> 3;
+        const int chunks = aborted ? 0 : (phase + p.hidden + 7) >> 3;  // an aborted warp touches nothing
         const uint32_t stage = smem_base + static_cast<uint32_t>(s) * p.stage_bytes;
         const int weight_shift = phase - p.row_phase;
 
@@ -437,7 +465,12 @@ __global__ void __launch_bounds__(kStagedThreads, 1) rmsnorm_staged_kernel(const
 #pragma unroll
             for (int w = 0; w < kWarpsPerRow; ++w) sumsq += slot[w];
             parity_slot ^= 1;
+            // A partner that gave up before the barrier set the abort flag first, so after the
+            // barrier every warp of the group sees it and drops the row (its partial sum is
+            // missing): the group decides together.
+            aborted = __any_sync(0xffffffffu, aborted || *abort != 0);
         }
+        if (aborted) continue;  // no pass 2, no release; the next row's barrier is still reached
         const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
         const F32x2 inv2 = f32x2_make(inv, inv);
 
@@ -603,11 +636,7 @@ __device__ __forceinline__ U32x4 load_weight_chunk(const uint16_t* weight, int c
     return w;
 }
 constexpr int kCtaRowMaxHidden = 4 * 8 * kCtaRowMaxThreads;  // 16384: four chunks per thread
-#ifdef IPL_TUNING_CTA_ROWS
-constexpr int64_t kCtaRowMaxRows = IPL_TUNING_CTA_ROWS;
-#else
 constexpr int64_t kCtaRowMaxRows = 256;
-#endif
 // Registers of the one-chunk instances (H <= 4096), held there by their launch bound, so the
 // planner can tell how many of their CTAs an SM holds at once: the bf16 ops 40, the fp8 op 64.
 constexpr int kRegistersPerSm = 65536;
@@ -623,7 +652,6 @@ constexpr unsigned kGammaPrefetchCtas = 148;
 // as the staged kernel's prefetch: L2 is where every SM's accesses meet.
 template <bool kResidual>
 __device__ __forceinline__ void prefetch_first_row(const WarpRowParams& p) {
-#ifndef IPL_TUNING_NO_PREFETCH
     if (threadIdx.x == 0 && static_cast<int64_t>(blockIdx.x) < p.rows) {
         const int64_t row = blockIdx.x;
         const uint32_t bytes = 2u * static_cast<uint32_t>(p.hidden);
@@ -633,7 +661,6 @@ __device__ __forceinline__ void prefetch_first_row(const WarpRowParams& p) {
         // every row's pass 2 waits on it. The first CTAs are enough: later ones find it in L2.
         if (blockIdx.x < kGammaPrefetchCtas) prefetch_span_l2(p.weight, bytes);
     }
-#endif
 }
 
 template <int kChunks, int kMode>
@@ -890,7 +917,6 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_shifted_kernel(co
     const float hidden_f = static_cast<float>(p.hidden);
     const bool weight_aligned = (reinterpret_cast<uintptr_t>(p.weight) & 15u) == 0;
 
-#ifndef IPL_TUNING_NO_PREFETCH
     if (threadIdx.x == 0 && static_cast<int64_t>(blockIdx.x) < p.rows) {
         const int64_t row = blockIdx.x;
         const uint32_t bytes = 2u * static_cast<uint32_t>(p.hidden);
@@ -898,7 +924,6 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_shifted_kernel(co
         if constexpr (kResidual) prefetch_span_l2(p.residual + row * p.hidden, bytes);
         if (blockIdx.x < kGammaPrefetchCtas) prefetch_span_l2(p.weight, bytes);
     }
-#endif
     grid_dependency_wait();
     grid_launch_dependents();
 

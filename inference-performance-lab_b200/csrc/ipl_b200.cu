@@ -60,6 +60,26 @@ ipl_status current_device(int* device, DeviceInfo** info) {
     return IPL_SUCCESS;
 }
 
+// Limits the plan queries plan with: the current device's, as the launch path reads them, so a
+// query names the kernel a call on this device launches. Where no device can be queried (a host
+// without a GPU), a B200's: 148 SMs, 232448 bytes of opt-in shared memory per block. Leaves
+// neither this thread's last-error message nor CUDA's last error changed.
+void plan_limits(int* sm_count, int* smem_limit) {
+    char saved[sizeof(t_last_error)];
+    std::memcpy(saved, t_last_error, sizeof(saved));
+    int device = 0;
+    DeviceInfo* info = nullptr;
+    if (current_device(&device, &info) == IPL_SUCCESS) {
+        *sm_count = info->sm_count.load(std::memory_order_relaxed);
+        *smem_limit = info->max_smem_optin.load(std::memory_order_relaxed);
+        return;
+    }
+    std::memcpy(t_last_error, saved, sizeof(saved));
+    (void)cudaGetLastError();
+    *sm_count = 148;
+    *smem_limit = 232448;
+}
+
 template <typename Kernel, typename... Args>
 cudaError_t launch(Kernel kernel, unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
                    Args... args) {
@@ -173,10 +193,6 @@ ipl_status check_rms_args(const void* x, const void* other, const void* weight, 
     return IPL_SUCCESS;
 }
 
-// Sweep builds that compare the choices below on a GPU may define IPL_TUNING_FAMILY (1 CTA per
-// row, 2 stash, 3 staged), IPL_TUNING_CTA_ROWS, IPL_TUNING_FORCE_GROUPS, IPL_TUNING_FORCE_STAGES or
-// IPL_TUNING_NO_PREFETCH; build.py defines none of them.
-//
 // Pure function of the arguments and two device limits. `other` is the residual (fused modes) or
 // the output (plain mode); either must share x's offset modulo 16 bytes for the staged kernel.
 // `out8` is the fp8 output of kModeFusedFp8, whose vector paths need 16-byte aligned rows
@@ -243,11 +259,7 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         plan.smem = static_cast<size_t>(hidden) * 4u;
         return plan;
     }
-#if defined(IPL_TUNING_FAMILY)
-    const int family_choice = IPL_TUNING_FAMILY;  // 1 CTA per row, 2 stash, 3 staged
-#else
-    const int family_choice = few_rows ? 1 : hidden > kStashMaxHidden ? 3 : 2;
-#endif
+    const int family_choice = few_rows ? 1 : hidden > kStashMaxHidden ? 3 : 2;  // 1 CTA per row, 2 stash, 3 staged
     // Rows of 16384 < H <= 32768: the stash kernel with eight chunks a thread (up to 512 threads;
     // add+RMSNorm and the fp8 op at 128 registers, one CTA an SM, or, up to H = 20480 and for more
     // than 256 rows, the instance capped at 96 registers, two an SM). 2-9x the two-pass row kernel that
@@ -328,12 +340,6 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
             }
             stages = groups;
         }
-#ifdef IPL_TUNING_FORCE_GROUPS
-        groups = IPL_TUNING_FORCE_GROUPS;
-#endif
-#ifdef IPL_TUNING_FORCE_STAGES
-        if (stages > IPL_TUNING_FORCE_STAGES) stages = IPL_TUNING_FORCE_STAGES;
-#endif
         plan.family = RmsFamily::kStaged;
         plan.warps_per_row = kStagedConsumerWarps / groups;
         plan.grid = static_cast<unsigned>(grid);
@@ -750,14 +756,17 @@ ipl_status ipl_clear_device_fault_flags(int device) {
 const char* ipl_fused_add_rms_norm_plan(const void* x, const void* residual, const void* weight, int64_t rows,
                                         int64_t hidden_size) {
     if (check_rms_args(x, residual, weight, rows, hidden_size, 1.0, true) != IPL_SUCCESS) return "invalid";
-    // B200 limits: 148 SMs, 232448 bytes of opt-in shared memory per block.
-    return rms_kernel_name(plan_rms(x, residual, nullptr, rows, hidden_size, kModeFused, 148, 232448), kModeFused);
+    int sms = 0, smem = 0;
+    plan_limits(&sms, &smem);
+    return rms_kernel_name(plan_rms(x, residual, nullptr, rows, hidden_size, kModeFused, sms, smem), kModeFused);
 }
 
 const char* ipl_rms_norm_plan(const void* output, const void* input, const void* weight, int64_t rows,
                               int64_t hidden_size) {
     if (check_rms_args(input, output, weight, rows, hidden_size, 1.0, false) != IPL_SUCCESS) return "invalid";
-    return rms_kernel_name(plan_rms(input, output, nullptr, rows, hidden_size, kModePlain, 148, 232448), kModePlain);
+    int sms = 0, smem = 0;
+    plan_limits(&sms, &smem);
+    return rms_kernel_name(plan_rms(input, output, nullptr, rows, hidden_size, kModePlain, sms, smem), kModePlain);
 }
 
 const char* ipl_fused_add_rms_norm_static_fp8_quant_plan(const void* output, const void* input, const void* residual,
@@ -765,7 +774,9 @@ const char* ipl_fused_add_rms_norm_static_fp8_quant_plan(const void* output, con
     if (check_rms_args(input, residual, weight, rows, hidden_size, 1.0, true) != IPL_SUCCESS || output == nullptr) {
         return "invalid";
     }
-    return rms_kernel_name(plan_rms(input, residual, output, rows, hidden_size, kModeFusedFp8, 148, 232448),
+    int sms = 0, smem = 0;
+    plan_limits(&sms, &smem);
+    return rms_kernel_name(plan_rms(input, residual, output, rows, hidden_size, kModeFusedFp8, sms, smem),
                            kModeFusedFp8);
 }
 

@@ -17,11 +17,16 @@ constexpr int kWarpSize = 32;
 // Fault bits stored in the per-device fault word (see ipl_device_fault_flags).
 constexpr uint32_t kFaultFullBarrierTimeout = 1u << 0;   // a consumer never saw its stage fill
 constexpr uint32_t kFaultEmptyBarrierTimeout = 1u << 1;  // the producer never saw a stage drain
+constexpr uint32_t kFaultCopyDrainTimeout = 1u << 2;     // a copy the producer issued never landed
 
 // Bounded waits give up after this long (nanoseconds of %globaltimer). A stage fills within
 // microseconds on a healthy GPU; the bound only exists so that a lost copy ends the kernel
-// with a recorded fault instead of a hang.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// with a recorded fault instead of a hang. Test builds shorten it (IPL_WAIT_LIMIT_NS) so that a
+// test can make a wait run out quickly.
+#ifndef IPL_WAIT_LIMIT_NS
+#define IPL_WAIT_LIMIT_NS 2000000000ull
+#endif
+constexpr uint64_t kWaitLimitNs = IPL_WAIT_LIMIT_NS;
 
 // Per-device fault word (read by ipl_device_fault_flags). Defined here: the library is a single
 // translation unit (ipl_b200.cu includes every kernel header).
@@ -232,6 +237,21 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
         if (global_timer_ns() - start > kWaitLimitNs) {
             atomicOr(&g_fault_word, fault_bit);
             *abort = 1;
+            return false;
+        }
+    }
+}
+
+// Waits for the phase with the given parity to complete, bounded by kWaitLimitNs only (not by
+// the abort flag): used to let copies already issued land before their CTA exits. Records
+// `fault_bit` and returns false when the limit passes.
+__device__ __forceinline__ bool mbar_wait_timed(uint32_t bar, uint32_t parity, uint32_t fault_bit) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = global_timer_ns();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (global_timer_ns() - start > kWaitLimitNs) {
+            atomicOr(&g_fault_word, fault_bit);
             return false;
         }
     }

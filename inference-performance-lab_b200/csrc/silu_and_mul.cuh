@@ -73,37 +73,37 @@ __global__ void __launch_bounds__(kSiluThreads) silu_vector_kernel(const SiluVec
     constexpr int kElems = kBytes / 2;
     constexpr int kWords = kBytes / 4;
     using Vec = typename std::conditional<kBytes == 32, U32x8, U32x4>::type;
-    const uint32_t stride = gridDim.x * blockDim.x;
-#ifndef IPL_TUNING_NO_PREFETCH
+    // Pack indices run in 64 bits: total_packs may be any 32-bit count, and base + stride * kUnroll
+    // must not wrap past it. A pack below total_packs fits 32 bits for the division.
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    const uint64_t first = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     // While the previous kernel in the stream drains, ask L2 for this thread's first packs of
     // gate and up (a prefetch only warms L2, where every SM's accesses meet, so the loads after
     // the wait still see the previous kernel's writes).
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
-        const uint32_t pack = blockIdx.x * blockDim.x + threadIdx.x + k * stride;
+        const uint64_t pack = first + k * stride;
         if (pack < p.total_packs) {
-            const uint32_t row = fast_div(pack, p.packs_per_row);
-            const uint32_t col = pack - row * p.packs_per_row.divisor;
+            const uint32_t row = fast_div(static_cast<uint32_t>(pack), p.packs_per_row);
+            const uint32_t col = static_cast<uint32_t>(pack) - row * p.packs_per_row.divisor;
             const uint16_t* gate = p.in + static_cast<int64_t>(row) * 2 * p.intermediate + int64_t{col} * kElems;
             prefetch_l2(gate);
             prefetch_l2(gate + p.intermediate);
         }
     }
-#endif
     grid_dependency_wait();
     grid_launch_dependents();
 
-    for (uint32_t base = blockIdx.x * blockDim.x + threadIdx.x; base < p.total_packs;
-         base += stride * kUnroll) {
+    for (uint64_t base = first; base < p.total_packs; base += stride * kUnroll) {
         Vec gate[kUnroll], up[kUnroll];
         int64_t out_off[kUnroll];
 #pragma unroll
         for (int k = 0; k < kUnroll; ++k) {
-            const uint32_t pack = base + k * stride;
+            const uint64_t pack = base + k * stride;
             out_off[k] = -1;
             if (pack < p.total_packs) {
-                const uint32_t row = fast_div(pack, p.packs_per_row);
-                const uint32_t col = pack - row * p.packs_per_row.divisor;
+                const uint32_t row = fast_div(static_cast<uint32_t>(pack), p.packs_per_row);
+                const uint32_t col = static_cast<uint32_t>(pack) - row * p.packs_per_row.divisor;
                 const int64_t in_off = static_cast<int64_t>(row) * 2 * p.intermediate + int64_t{col} * kElems;
                 out_off[k] = static_cast<int64_t>(row) * p.intermediate + int64_t{col} * kElems;
                 if constexpr (kBytes == 32) {

@@ -5,7 +5,7 @@ Imports ``src/inference_performance_lab/kernels/reference.py`` of sreeganeshji/i
 inputs and stores inputs and outputs as raw bf16 bit patterns (uint16) in ``golden.npz``.
 The checkout is only needed to regenerate; the tests read the committed ``golden.npz``.
 
-    python tests/golden/make_golden.py [--reference /path/to/inference-performance-lab]
+    python tests/golden/make_golden.py --reference /path/to/inference-performance-lab
 
 Cases follow the reference's input recipes: x = randn, residual = randn_like(x),
 weight = randn(H) * 0.1 + 1.0 in bf16 (tests/test_fused_add_rms_norm.py:20-24), SiLU input
@@ -50,7 +50,7 @@ def rms_inputs(rows: int, hidden: int, seed: int, scale: float = 1.0):
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    parser.add_argument("--reference", type=Path, required=True, help="root of the reference checkout")
     args = parser.parse_args()
     ref = load_reference(args.reference)
 

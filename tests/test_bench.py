@@ -1,5 +1,6 @@
 """bench.py's command-line contract, on the CPU: the reference arm's JSON line, rank handling under
-a two-rank launch, the warm-up floor, and our arm refusing to run without a GPU (no fallback)."""
+a two-rank launch, the warm-up floor, the gloo control plane, and our arm refusing to run without a
+GPU (no fallback); on a GPU, our arm's full line with its sub-records."""
 
 from __future__ import annotations
 
@@ -74,8 +75,20 @@ def test_our_arm_prints_the_full_contract_line_on_a_gpu() -> None:
     rl = d["roofline"]
     assert rl["bound"] == "hbm" and rl["unit"] == "GB/s" and rl["peak"] > 0
     assert abs(rl["frac"] - rl["achieved"] / rl["peak"]) < 1e-9 and 0.3 < rl["frac"] < 1.2
+    assert rl["traffic"] is None or rl["traffic_ratio"] == rl["traffic"] / d["config"]["bytes_per_step_per_rank"]
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] > 0
     e2e = d["e2e"]
     assert e2e["h2d_bytes_per_step"] == e2e["d2h_bytes_per_step"] == 2048 * 3584 * 2 * 2 and e2e["value"] > 0
     assert d["gpu_launches"] == 20
     assert {"sm_mhz", "sm_max_mhz", "reasons"} <= set(d["clocks"])
+    # Every launch was queued before the region started, and the host's pace is reported beside it.
+    assert d["launch"]["queued_before_start"] and d["launch"]["host_us_per_call"] > 0
+    assert d["parity"]["parity_ok"] and d["parity"]["residual_exact"] and d["parity"]["rows_checked"] == 2048
+    # The other three workloads, measured in the same run and checked against the oracle.
+    for key, kernel_prefix in (("sharded", "rmsnorm_stash_kernel"), ("misaligned", "rmsnorm_shifted_kernel"),
+                               ("silu", "silu_vector_kernel")):
+        sub = d[key]
+        assert sub["kernel"].startswith(kernel_prefix), (key, sub["kernel"])
+        assert sub["parity"]["parity_ok"] and sub["parity"]["parity_ok_all_ranks"], (key, sub["parity"])
+        assert sub["value"] > 0 and 0.1 < sub["roofline_frac"] < 1.3 and sub["launch"]["queued_before_start"]
+    assert d["sharded"]["rows_per_rank"] == 262144 and d["sharded"]["parity"]["rows_checked"] >= 64

@@ -116,7 +116,7 @@ def _failing_rank_worker(rank: int, world: int, port: int, queue) -> None:
                       LOCAL_RANK=str(rank))
     import bench
 
-    d = bench.Dist(use_gpu=False, timeout_s=5.0)
+    d = bench.Dist(timeout_s=5.0)
     d.barrier()  # step 1 completes on both ranks
     if rank == 1:
         raise RuntimeError("rank 1 fails between steps")
@@ -146,3 +146,43 @@ def test_failed_rank_ends_the_others_barrier() -> None:
     assert outcome != "no error"
     assert waited < 30.0
     assert procs[1].exitcode not in (0, None) and procs[0].exitcode == 3
+
+
+def _control_plane_worker(rank: int, world: int, port: int, queue) -> None:
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import bench
+
+    d = bench.Dist(timeout_s=30.0)
+    try:
+        d.barrier()
+        elapsed = d.max(1.5 * (rank + 1))
+        verdict = d.all(rank != 1)
+        per_rank = d.gather({"rank": rank, "us": 10.0 + rank})
+        if rank == 0:
+            queue.put((d.pg.get_backend(), elapsed, verdict, per_rank))
+    finally:
+        d.close()
+
+
+def test_bench_control_plane_is_gloo_on_the_host() -> None:
+    """bench.py's timing control plane (barrier, max over ranks, the parity verdict, per-rank
+    records) runs on a gloo group of host tensors: no NCCL and no device collective."""
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_control_plane_worker, args=(rank, 2, port, queue)) for rank in range(2)]
+    for p in procs:
+        p.start()
+    backend, elapsed, verdict, per_rank = queue.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert backend == "gloo"
+    assert elapsed == 3.0
+    assert verdict is False  # one rank's failed check fails the run
+    assert [r["rank"] for r in per_rank] == [0, 1] and per_rank[1]["us"] == 11.0
