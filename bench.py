@@ -24,11 +24,13 @@ Unless ``--no-subrecords``, the line for the default workload also carries ``sha
 ``misaligned`` and ``silu`` records: the other three workloads measured the same way in the same
 run, each with its kernel, timings, roofline fraction and an oracle check of its outputs.
 
-Timing: W warm-up steps, then the K steps are enqueued while the device is held by a short sleep
-kernel placed before the start event (NVBench's blocking-kernel method), so the timed region is
-the device running the K launches back to back, not the host's pace of enqueuing them. The host's
-cost per call, whether all K launches were queued before the region started, the same K steps
-launched just in time (no hold) and a CUDA-graph replay of them are reported beside it.
+Timing: W warm-up steps; then, while the device is held by a short sleep kernel (NVBench's
+blocking-kernel method), the host enqueues W more warm-up steps, the start event, the K timed
+steps and the end event. The timed region is the device running the K launches back to back
+right after W launches that bring HBM and L2 to their steady state, not the host's pace of
+enqueuing them. The host's cost per call, whether all K launches were queued before the region
+started, the same K steps launched just in time (no hold) and a CUDA-graph replay of the same
+launches are reported beside it.
 
 Metric: algorithmic HBM bytes per step (add+RMSNorm: 4*H*2 per row = read x, r + write x, r;
 weight excluded; SiLU: 6 per output element) over the device time, in GB/s, summed over ranks.
@@ -474,12 +476,14 @@ class OpWorkload:
 def time_calls(calls, steps: int, warmup: int, stream, dist, clocks: ClockSampler | None) -> dict:
     """W warm-up calls, then K calls timed on the device.
 
-    The K launches are enqueued while the device sleeps in a hold kernel issued before the start
-    event, so the events bracket the device running them back to back (the host's enqueue pace is
-    reported separately as ``host_us_per_call``). ``queued_before_start`` says whether every launch
-    was in the queue before the start event fired. The same K calls are then run again without
-    the hold, as a caller that launches just in time would: ``unqueued_us_per_step``, and
-    ``idle_us_per_step``, the device time per step that the host's pace adds."""
+    The device is held by a short sleep kernel while the host enqueues W more warm-up calls, the
+    start event and the K timed calls (NVBench's blocking-kernel method): the events then bracket
+    the device running the K launches back to back, right after W launches that bring the memory
+    system to its steady state, and the host's enqueue pace is reported separately
+    (``host_us_per_call``). ``queued_before_start`` says whether every timed launch was in the
+    queue before the start event fired. The same K calls are then run again without the hold, as
+    a caller that launches just in time would: ``unqueued_us_per_step``, and ``idle_us_per_step``,
+    the device time per step that the host's pace adds."""
     import torch
 
     n = len(calls)
@@ -487,16 +491,19 @@ def time_calls(calls, steps: int, warmup: int, stream, dist, clocks: ClockSample
     for i in range(warmup):
         calls[i % n]()
     host_warm = (time.perf_counter() - t0) / max(warmup, 1)
+    pre = [calls[i % n] for i in range(warmup)]
     order = [calls[(warmup + i) % n] for i in range(steps)]
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
-    hold_s = min(max(50e-6, 2.0 * steps * host_warm + 20e-6), 0.2)
+    hold_s = min(max(50e-6, 2.0 * (steps + warmup) * host_warm + 20e-6), 0.2)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if clocks is not None:
         clocks.__enter__()
     try:
         torch.cuda._sleep(int(hold_s * HOLD_CLOCK_GHZ * 1e9))
+        for call in pre:
+            call()
         start.record(stream)
         h0 = time.perf_counter()
         for call in order:
@@ -534,14 +541,13 @@ def time_calls(calls, steps: int, warmup: int, stream, dist, clocks: ClockSample
     }
 
 
-def graph_replay_us(calls, steps: int, stream) -> float:
-    """Per-launch device time of the same launches replayed from a CUDA graph (launch cost gone)."""
+def graph_replay_us(calls, stream) -> float:
+    """Per-launch device time of the same launches replayed from a CUDA graph of at least 100 of
+    them (launch cost gone), timed on a replay that directly follows an untimed one."""
     import torch
 
     sets = len(calls)
-    graph_steps = min(max(steps, sets), 100 * sets)
-    graph_steps -= graph_steps % sets
-    graph_steps = max(graph_steps, sets)
+    graph_steps = max(sets, -(-100 // sets) * sets)
     graph = torch.cuda.CUDAGraph()
     capture_stream = torch.cuda.Stream()
     capture_stream.wait_stream(stream)
@@ -552,14 +558,13 @@ def graph_replay_us(calls, steps: int, stream) -> float:
     stream.wait_stream(capture_stream)
     graph.replay()
     torch.cuda.synchronize()
-    replays = max(1, steps // graph_steps)
     g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    graph.replay()
     g0.record(stream)
-    for _ in range(replays):
-        graph.replay()
+    graph.replay()
     g1.record(stream)
     g1.synchronize()
-    us = g0.elapsed_time(g1) / (replays * graph_steps) * 1e3
+    us = g0.elapsed_time(g1) / graph_steps * 1e3
     del graph
     return us
 
@@ -589,7 +594,7 @@ def measure_workload(name: str, spec, dist, device, stream, steps: int, warmup: 
     calls = [workload.bind(batch, shared) for batch in batches]
     clocks = ClockSampler(dist.local_rank)
     timing = time_calls(calls, steps, warmup, stream, dist, clocks)
-    graph_us = graph_replay_us(calls, steps, stream) if graph else None
+    graph_us = graph_replay_us(calls, stream) if graph else None
     kernel = workload.plan(batches[0], shared, rows) if with_plan else None
     peak, peak_kind = load_peak()
     local_us = timing["local_ms"] / steps * 1e3

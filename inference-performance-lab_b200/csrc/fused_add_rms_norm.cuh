@@ -536,6 +536,9 @@ struct WarpRowParams {
     int64_t rows;
     int hidden;
     float epsilon;
+    // Stash and shifted kernels: the CTAs the GPU holds at once for this launch (one resident
+    // wave) when the launch has rows beyond it, else 0. See prefetch_next_wave_row.
+    int64_t lookahead;
 };
 
 template <int kChunks, int kMode>
@@ -660,6 +663,27 @@ __device__ __forceinline__ void prefetch_first_row(const WarpRowParams& p) {
         // Gamma too (each layer of a model has its own, cold in L2 by the time it runs again);
         // every row's pass 2 waits on it. The first CTAs are enough: later ones find it in L2.
         if (blockIdx.x < kGammaPrefetchCtas) prefetch_span_l2(p.weight, bytes);
+    }
+}
+
+// After its dependency wait, a CTA of the first resident wave (blockIdx < lookahead) asks L2 for
+// row blockIdx + lookahead, one that a CTA of the following wave will load. A launch of a few
+// waves otherwise runs out of DRAM requests once its first wave's loads have returned: the first
+// wave's rows were prefetched before the wait and arrive from L2, while the second wave's CTAs
+// issue their loads only as the first wave's CTAs retire. With the look-ahead the second wave's
+// rows stream from HBM while the first wave computes. Issued after the wait, it cannot race the
+// previous kernel's writes, and it competes with no earlier launch's traffic. Only the first wave
+// asks, so a launch of many waves prefetches one wave early and then runs as before. Measured on
+// B200 (cold, CUDA graph, fused op): 2048 x 3584 9.41 against 10.40 us, 4096 x 3584 17.45 against
+// 18.78; a distance of two waves at 262144 x 8192 thrashed L2 (3056 against 2468 us), hence one.
+template <bool kResidual>
+__device__ __forceinline__ void prefetch_next_wave_row(const WarpRowParams& p) {
+    if (threadIdx.x == 0 && static_cast<int64_t>(blockIdx.x) < p.lookahead &&
+        static_cast<int64_t>(blockIdx.x) + p.lookahead < p.rows) {
+        const int64_t row = static_cast<int64_t>(blockIdx.x) + p.lookahead;
+        const uint32_t bytes = 2u * static_cast<uint32_t>(p.hidden);
+        prefetch_span_l2(p.x + row * p.hidden, bytes);
+        if constexpr (kResidual) prefetch_span_l2(p.residual + row * p.hidden, bytes);
     }
 }
 
@@ -797,6 +821,7 @@ __global__ void __launch_bounds__(kCapped ? kStashCappedThreads : kStashMaxThrea
     prefetch_first_row<kResidual>(p);
     grid_dependency_wait();
     grid_launch_dependents();
+    prefetch_next_wave_row<kResidual>(p);
     const float scale_inv = kFp8 ? 1.0f / *p.scale : 1.0f;
     const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
 
@@ -926,6 +951,7 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_shifted_kernel(co
     }
     grid_dependency_wait();
     grid_launch_dependents();
+    prefetch_next_wave_row<kResidual>(p);
 
     int parity = 0;
     for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {

@@ -110,6 +110,7 @@ struct RmsPlan {
     unsigned threads = 0;     // CTA-per-row and stash kernels: block size
     bool capped = false;      // stash kernel, rows of 16384 < H <= 20480: the 96-register instance
     int phase = 0;            // shifted kernel: elements from the 16-byte block to each row
+    int64_t lookahead = 0;    // stash and shifted kernels: one resident wave, when rows exceed it
     unsigned grid = 0;
     size_t smem = 0;
     StagedParams staged = {};
@@ -191,6 +192,16 @@ ipl_status check_rms_args(const void* x, const void* other, const void* weight, 
         return fail(IPL_ERROR_INVALID_VALUE, "x and residual must not alias");
     }
     return IPL_SUCCESS;
+}
+
+// CTAs of `threads` threads that the GPU holds at once when each thread may take `regs`
+// registers (the cap the kernel's launch bound sets; allocation is in whole multiples of 8, which
+// 64, 96 and 128 are): the register file, threads per SM and 32 CTAs per SM all bound it.
+int64_t resident_ctas(int sm_count, int64_t threads, int64_t regs) {
+    int64_t per_sm = kRegistersPerSm / (threads * regs);
+    if (per_sm > kThreadsPerSm / threads) per_sm = kThreadsPerSm / threads;
+    if (per_sm > 32) per_sm = 32;
+    return static_cast<int64_t>(sm_count) * per_sm;
 }
 
 // Pure function of the arguments and two device limits. `other` is the residual (fused modes) or
@@ -285,6 +296,8 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         plan.phase = static_cast<int>((xa & 15u) >> 1);
         plan.threads = static_cast<unsigned>(threads);
         plan.grid = static_cast<unsigned>(rows < INT_MAX ? rows : INT_MAX);
+        const int64_t wave = resident_ctas(sm_count, threads, 64);  // launch bound (512, 2): 64 registers
+        plan.lookahead = rows > wave ? wave : 0;
         return plan;
     }
     // Many aligned rows: a small CTA for every row, each thread's chunks in registers.
@@ -302,6 +315,11 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         plan.threads = static_cast<unsigned>(threads);
         plan.smem = 0;
         plan.grid = static_cast<unsigned>(rows < INT_MAX ? rows : INT_MAX);
+        // Registers a thread may take under each instance's launch bound: 64, the capped
+        // instance 96, eight chunks a thread with a residual 128.
+        const int64_t regs = plan.capped ? 96 : (per_lane == kStashWideChunks && mode != kModePlain) ? 128 : 64;
+        const int64_t wave = resident_ctas(sm_count, threads, regs);
+        plan.lookahead = rows > wave ? wave : 0;
         return plan;
     }
     // Few aligned rows: a CTA per row, values in registers.
@@ -358,6 +376,21 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
     const int64_t cap = static_cast<int64_t>(sm_count) * 8;
     plan.grid = static_cast<unsigned>(rows < cap ? rows : cap);
     return plan;
+}
+
+WarpRowParams row_params(const RmsPlan& plan) {
+    WarpRowParams w;
+    w.x = plan.staged.x;
+    w.residual = plan.staged.residual;
+    w.out = plan.staged.out;
+    w.out8 = plan.staged.out8;
+    w.scale = plan.staged.scale;
+    w.weight = plan.staged.weight;
+    w.rows = plan.staged.rows;
+    w.hidden = plan.staged.hidden;
+    w.epsilon = plan.staged.epsilon;
+    w.lookahead = plan.lookahead;
+    return w;
 }
 
 const char* mode_label(int mode) {
@@ -424,6 +457,8 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8
     plan.staged.out8 = out8;
     plan.staged.scale = scale;
     plan.staged.weight = weight;
+    plan.staged.rows = rows;
+    plan.staged.hidden = static_cast<int>(hidden);
     plan.staged.epsilon = static_cast<float>(epsilon);
     switch (plan.family) {
         case RmsFamily::kStaged:
@@ -439,16 +474,7 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8
                 }
             }
         case RmsFamily::kWarpRow: {
-            WarpRowParams w;
-            w.x = x;
-            w.residual = residual;
-            w.out = out;
-            w.out8 = out8;
-            w.scale = scale;
-            w.weight = weight;
-            w.rows = rows;
-            w.hidden = static_cast<int>(hidden);
-            w.epsilon = plan.staged.epsilon;
+            const WarpRowParams w = row_params(plan);
             cudaError_t err = cudaSuccess;
             switch (plan.chunks_per_lane) {
                 case 1: err = launch(rmsnorm_warp_kernel<1, kMode>, plan.grid, kWarpRowThreads, plan.smem, stream, w); break;
@@ -461,16 +487,7 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8
             return IPL_SUCCESS;
         }
         case RmsFamily::kCtaRow: {
-            WarpRowParams w;
-            w.x = x;
-            w.residual = residual;
-            w.out = out;
-            w.out8 = out8;
-            w.scale = scale;
-            w.weight = weight;
-            w.rows = rows;
-            w.hidden = static_cast<int>(hidden);
-            w.epsilon = plan.staged.epsilon;
+            const WarpRowParams w = row_params(plan);
             cudaError_t err = cudaSuccess;
             switch (plan.chunks_per_lane) {
                 case 1: err = launch(rmsnorm_cta_kernel<1, kMode>, plan.grid, plan.threads, 0, stream, w); break;
@@ -483,32 +500,14 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8
             return IPL_SUCCESS;
         }
         case RmsFamily::kStash: {
-            WarpRowParams w;
-            w.x = x;
-            w.residual = residual;
-            w.out = out;
-            w.out8 = out8;
-            w.scale = scale;
-            w.weight = weight;
-            w.rows = rows;
-            w.hidden = static_cast<int>(hidden);
-            w.epsilon = plan.staged.epsilon;
+            const WarpRowParams w = row_params(plan);
             return launch_stash<kMode>(plan, stream, w);
         }
         case RmsFamily::kShifted: {
             if constexpr (kMode == kModeFusedFp8) {
                 return fail(IPL_ERROR_CUDA, "%s: no shifted plan exists for this mode", mode_label(kMode));
             } else {
-                WarpRowParams w;
-                w.x = x;
-                w.residual = residual;
-                w.out = out;
-                w.out8 = out8;
-                w.scale = scale;
-                w.weight = weight;
-                w.rows = rows;
-                w.hidden = static_cast<int>(hidden);
-                w.epsilon = plan.staged.epsilon;
+                const WarpRowParams w = row_params(plan);
                 cudaError_t err = cudaSuccess;
                 switch (plan.phase) {
                     case 1: err = launch(rmsnorm_shifted_kernel<kMode, 1>, plan.grid, plan.threads, 0, stream, w); break;

@@ -58,7 +58,7 @@ def _inputs(rows: int, hidden: int, seed: int):
 
 @pytest.mark.parametrize(
     ("rows", "hidden"),
-    [(64, 1000), (1000, 1000), (600, 16001)],
+    [(64, 1001), (1000, 1001), (600, 16001)],
     ids=["row-per-cta", "rows-in-own-stages", "streaming-ring"],
 )
 def test_staged_wait_runs_out_and_the_kernel_returns(rows: int, hidden: int) -> None:
@@ -98,9 +98,11 @@ def test_context_stays_usable_after_a_wait_ran_out() -> None:
     require_cuda()
     torch.cuda.set_device(0)
     lib = _library()
-    x, r, w = _inputs(64, 1000, seed=1)
+    x, r, w = _inputs(64, 1001, seed=1)
     stream = torch.cuda.current_stream().cuda_stream
-    assert lib.ipl_fused_add_rms_norm_bf16(x.data_ptr(), r.data_ptr(), w.data_ptr(), 64, 1000, 1e-6, stream) == 0
+    assert lib.ipl_fused_add_rms_norm_plan(x.data_ptr(), r.data_ptr(), w.data_ptr(), 64, 1001).decode() \
+        .startswith("rmsnorm_staged_kernel<")
+    assert lib.ipl_fused_add_rms_norm_bf16(x.data_ptr(), r.data_ptr(), w.data_ptr(), 64, 1001, 1e-6, stream) == 0
     torch.cuda.synchronize()
     assert _flags(lib) & FAULT_FULL_BARRIER_TIMEOUT
     assert lib.ipl_clear_device_fault_flags(0) == 0
