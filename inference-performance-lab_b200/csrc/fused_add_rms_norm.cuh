@@ -537,8 +537,10 @@ struct WarpRowParams {
     int hidden;
     float epsilon;
     // Stash and shifted kernels: the CTAs the GPU holds at once for this launch (one resident
-    // wave) when the launch has rows beyond it, else 0. See prefetch_next_wave_row.
+    // wave) when the launch has rows beyond it, else 0; and how many CTAs, from the first, ask L2
+    // for the row one wave ahead of theirs. See prefetch_next_wave_row.
     int64_t lookahead;
+    int64_t lookahead_ctas;
 };
 
 template <int kChunks, int kMode>
@@ -666,19 +668,23 @@ __device__ __forceinline__ void prefetch_first_row(const WarpRowParams& p) {
     }
 }
 
-// After its dependency wait, a CTA of the first resident wave (blockIdx < lookahead) asks L2 for
-// row blockIdx + lookahead, one that a CTA of the following wave will load. A launch of a few
-// waves otherwise runs out of DRAM requests once its first wave's loads have returned: the first
-// wave's rows were prefetched before the wait and arrive from L2, while the second wave's CTAs
-// issue their loads only as the first wave's CTAs retire. With the look-ahead the second wave's
-// rows stream from HBM while the first wave computes. Issued after the wait, it cannot race the
-// previous kernel's writes, and it competes with no earlier launch's traffic. Only the first wave
-// asks, so a launch of many waves prefetches one wave early and then runs as before. Measured on
-// B200 (cold, CUDA graph, fused op): 2048 x 3584 9.41 against 10.40 us, 4096 x 3584 17.45 against
-// 18.78; a distance of two waves at 262144 x 8192 thrashed L2 (3056 against 2468 us), hence one.
+// After its dependency wait, CTA b (b < lookahead_ctas) asks L2 for row b + lookahead, one wave
+// ahead: a row that a CTA of the following wave will load. A launch of a few waves otherwise runs
+// out of DRAM requests once its first wave's loads have returned: the first wave's rows were
+// prefetched before the wait and arrive from L2, while the next wave's CTAs issue their loads
+// only as the first wave's CTAs retire. With the look-ahead the next wave's rows stream from HBM
+// while the current wave computes. Issued after the wait, it cannot race the previous kernel's
+// writes, and it competes with no earlier launch's traffic. The planner lets every CTA ask in a
+// launch of up to four waves and only the first wave beyond that, where the extra requests only
+// compete with the demand loads. Measured on B200 (cold, CUDA graph, fused op, against no
+// look-ahead): 2048 x 3584 9.31 against 10.29 us, 1536 x 3584 8.14 against 8.68, every CTA at
+// 4096 x 3584 17.66 against 18.96 and at 2048 x 8192 20.28 against 21.93; at 8192 x 4096 every
+// CTA asking was 2 % slower and the first wave alone 3 % faster, at 32768 and 262144 x 8192 every
+// CTA 2 % slower and the first wave alone level; a distance of two waves thrashed L2 at
+// 262144 x 8192 (3056 against 2468 us), hence one.
 template <bool kResidual>
 __device__ __forceinline__ void prefetch_next_wave_row(const WarpRowParams& p) {
-    if (threadIdx.x == 0 && static_cast<int64_t>(blockIdx.x) < p.lookahead &&
+    if (threadIdx.x == 0 && static_cast<int64_t>(blockIdx.x) < p.lookahead_ctas &&
         static_cast<int64_t>(blockIdx.x) + p.lookahead < p.rows) {
         const int64_t row = static_cast<int64_t>(blockIdx.x) + p.lookahead;
         const uint32_t bytes = 2u * static_cast<uint32_t>(p.hidden);

@@ -110,7 +110,8 @@ struct RmsPlan {
     unsigned threads = 0;     // CTA-per-row and stash kernels: block size
     bool capped = false;      // stash kernel, rows of 16384 < H <= 20480: the 96-register instance
     int phase = 0;            // shifted kernel: elements from the 16-byte block to each row
-    int64_t lookahead = 0;    // stash and shifted kernels: one resident wave, when rows exceed it
+    int64_t lookahead = 0;       // stash and shifted kernels: one resident wave, when rows exceed it
+    int64_t lookahead_ctas = 0;  // ... and how many CTAs look one wave ahead
     unsigned grid = 0;
     size_t smem = 0;
     StagedParams staged = {};
@@ -202,6 +203,14 @@ int64_t resident_ctas(int sm_count, int64_t threads, int64_t regs) {
     if (per_sm > kThreadsPerSm / threads) per_sm = kThreadsPerSm / threads;
     if (per_sm > 32) per_sm = 32;
     return static_cast<int64_t>(sm_count) * per_sm;
+}
+
+// The one-wave look-ahead of the stash and shifted kernels (prefetch_next_wave_row): every CTA
+// looks ahead in a launch of up to four resident waves, the first wave only in a longer one.
+constexpr int64_t kLookaheadAllWaves = 4;
+void set_lookahead(RmsPlan& plan, int64_t rows, int64_t wave) {
+    plan.lookahead = rows > wave ? wave : 0;
+    plan.lookahead_ctas = rows > wave ? (rows <= kLookaheadAllWaves * wave ? rows : wave) : 0;
 }
 
 // Pure function of the arguments and two device limits. `other` is the residual (fused modes) or
@@ -296,8 +305,7 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         plan.phase = static_cast<int>((xa & 15u) >> 1);
         plan.threads = static_cast<unsigned>(threads);
         plan.grid = static_cast<unsigned>(rows < INT_MAX ? rows : INT_MAX);
-        const int64_t wave = resident_ctas(sm_count, threads, 64);  // launch bound (512, 2): 64 registers
-        plan.lookahead = rows > wave ? wave : 0;
+        set_lookahead(plan, rows, resident_ctas(sm_count, threads, 64));  // launch bound (512, 2): 64 registers
         return plan;
     }
     // Many aligned rows: a small CTA for every row, each thread's chunks in registers.
@@ -318,8 +326,7 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         // Registers a thread may take under each instance's launch bound: 64, the capped
         // instance 96, eight chunks a thread with a residual 128.
         const int64_t regs = plan.capped ? 96 : (per_lane == kStashWideChunks && mode != kModePlain) ? 128 : 64;
-        const int64_t wave = resident_ctas(sm_count, threads, regs);
-        plan.lookahead = rows > wave ? wave : 0;
+        set_lookahead(plan, rows, resident_ctas(sm_count, threads, regs));
         return plan;
     }
     // Few aligned rows: a CTA per row, values in registers.
@@ -390,6 +397,7 @@ WarpRowParams row_params(const RmsPlan& plan) {
     w.hidden = plan.staged.hidden;
     w.epsilon = plan.staged.epsilon;
     w.lookahead = plan.lookahead;
+    w.lookahead_ctas = plan.lookahead_ctas;
     return w;
 }
 

@@ -28,7 +28,9 @@ from parity import assert_bits_equal, assert_close_to_oracle, require_cuda
 pytestmark = pytest.mark.gpu
 
 WAIT_TEST_LIBRARY = NATIVE_DIR / "test" / "libipl_b200_waittest.so"
-FAULT_FULL_BARRIER_TIMEOUT = 1 << 0
+FAULT_FULL_BARRIER_TIMEOUT = 1 << 0   # a consumer gave up waiting for its row
+FAULT_EMPTY_BARRIER_TIMEOUT = 1 << 1  # the producer gave up waiting for a stage to be released
+FAULT_COPY_DRAIN_TIMEOUT = 1 << 2     # a copy the producer issued had not landed at its exit
 
 
 def _library() -> ctypes.CDLL:
@@ -57,11 +59,19 @@ def _inputs(rows: int, hidden: int, seed: int):
 
 
 @pytest.mark.parametrize(
-    ("rows", "hidden"),
-    [(64, 1001), (1000, 1001), (600, 16001)],
+    ("rows", "hidden", "expected_bits"),
+    [
+        # Every row has a stage of its own: only consumers wait, so a consumer gives up first.
+        (64, 1001, FAULT_FULL_BARRIER_TIMEOUT),
+        (1000, 1001, FAULT_FULL_BARRIER_TIMEOUT),
+        # Two stages: the producer, waiting for the never-filled stage to be released, and the
+        # consumers of that row, waiting for it to fill, start their waits microseconds apart;
+        # whichever gives up first records its bit and the others leave on the abort flag.
+        (600, 16001, FAULT_FULL_BARRIER_TIMEOUT | FAULT_EMPTY_BARRIER_TIMEOUT),
+    ],
     ids=["row-per-cta", "rows-in-own-stages", "streaming-ring"],
 )
-def test_staged_wait_runs_out_and_the_kernel_returns(rows: int, hidden: int) -> None:
+def test_staged_wait_runs_out_and_the_kernel_returns(rows: int, hidden: int, expected_bits: int) -> None:
     require_cuda()
     torch.cuda.set_device(0)
     lib = _library()
@@ -77,7 +87,9 @@ def test_staged_wait_runs_out_and_the_kernel_returns(rows: int, hidden: int) -> 
     assert status == 0, lib.ipl_last_error()
     torch.cuda.synchronize()  # the kernel returned and the context is intact
 
-    assert _flags(lib) & FAULT_FULL_BARRIER_TIMEOUT
+    flags = _flags(lib)
+    assert flags & expected_bits, f"fault word {flags:#x}"
+    assert not flags & ~expected_bits, f"fault word {flags:#x}"  # in particular no copy was left in flight
     # CTA b owns rows [rows * b // grid, rows * (b + 1) // grid), so CTA 0 rows [0, rows // grid);
     # its row 0 was never copied, so nothing wrote it.
     grid = min(rows, torch.cuda.get_device_properties(0).multi_processor_count)
