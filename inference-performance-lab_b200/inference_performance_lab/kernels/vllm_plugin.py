@@ -25,6 +25,17 @@ from inference_performance_lab.kernels.extension import rms_norm as custom_rms_n
 PROVIDER = "inference_lab"
 
 
+def _share_memory(a: Tensor, b: Tensor) -> bool:
+    """Whether a and b start at the same address. vLLM's Inductor lowering pass chooses the
+    provider on fake tensors, which carry no data (their data_ptr() reads 0 for every tensor):
+    there they are two distinct arguments of the IR op, so they do not alias."""
+    from torch._subclasses.fake_tensor import is_fake
+
+    if is_fake(a) or is_fake(b):
+        return False
+    return a.data_ptr() == b.data_ptr()
+
+
 def supports_fused_add_rms_norm(
     x: Tensor,
     x_residual: Tensor,
@@ -50,7 +61,7 @@ def supports_fused_add_rms_norm(
         and x.is_contiguous()
         and x_residual.is_contiguous()
         and weight.is_contiguous()
-        and x.data_ptr() != x_residual.data_ptr()
+        and not _share_memory(x, x_residual)
     )
 
 

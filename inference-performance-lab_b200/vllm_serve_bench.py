@@ -212,6 +212,8 @@ def run(args, provider: str, work: Path) -> dict:
         "--no-enable-prefix-caching", "--generation-config", "vllm", "--seed", "0",
         "--ir-op-priority", json.dumps(priority), "--host", "127.0.0.1", "--port", str(args.port),
     ]
+    if args.custom_ops:
+        command += ["--compilation-config", json.dumps({"custom_ops": args.custom_ops.split(",")})]
     if args.profile:
         command += ["--profiler-config", json.dumps({
             "profiler": "torch", "torch_profiler_dir": str(trace_dir), "torch_profiler_with_stack": False,
@@ -241,7 +243,8 @@ def run(args, provider: str, work: Path) -> dict:
     return {
         "provider": provider,
         "model": "Qwen2.5-7B architecture, 28 layers, dummy bf16 weights, word-level tokenizer of its vocabulary size",
-        "server": "vllm serve, default compilation (torch.compile + CUDA graphs), prefix caching off",
+        "server": "vllm serve, default compilation (torch.compile + CUDA graphs), prefix caching off"
+                  + (f", custom ops {args.custom_ops}" if args.custom_ops else ""),
         "ir_op_priority": priority,
         "vllm_plugins": env["VLLM_PLUGINS"],
         "startup_s": round(startup_s, 1),
@@ -264,6 +267,8 @@ def main() -> None:
     parser.add_argument("--port", type=int, default=8011)
     parser.add_argument("--startup-timeout", type=float, default=1200.0)
     parser.add_argument("--workdir", type=Path, default=Path("vllm_serve_work"))
+    parser.add_argument("--custom-ops", default=None,
+                        help='vLLM custom ops to enable under compilation, e.g. "+silu_and_mul" (default: vLLM\'s)')
     args = parser.parse_args()
     args.workdir.mkdir(parents=True, exist_ok=True)
     for provider in args.provider or ["vllm_c", "inference_lab"]:

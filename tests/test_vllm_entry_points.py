@@ -73,3 +73,28 @@ def test_vllm_loads_the_providers_through_the_entry_points(tmp_path: Path) -> No
     assert "inference_lab" in found["fused_add_rms_norm"] and "inference_lab" in found["rms_norm"]
     assert "SiluAndMul" in found["oot"]
     assert found["schema"].startswith("inference_performance_lab::fused_add_rms_norm(Tensor(a!) x")
+
+
+def test_provider_accepts_the_fake_tensors_of_inductor_lowering() -> None:
+    """Under vLLM's default compilation the IR lowering pass picks the provider by calling
+    supports_args on fake tensors (vllm/compilation/passes/ir/lowering_pass.py: dispatch(*fake_args))
+    and then traces the provider's function on them. Fake tensors carry no data pointer, so the
+    aliasing check must not reject them, and the op calls must trace; on real tensors the check
+    still rejects x and residual sharing memory."""
+    pytest.importorskip("vllm.ir")
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    from inference_performance_lab.kernels import extension, vllm_plugin
+
+    extension.load_extension()
+    with FakeTensorMode(allow_non_fake_inputs=True):
+        x = torch.empty(16, 3584, dtype=torch.bfloat16, device="cuda")
+        r = torch.empty(16, 3584, dtype=torch.bfloat16, device="cuda")
+        w = torch.empty(3584, dtype=torch.bfloat16, device="cuda")
+        assert vllm_plugin.supports_fused_add_rms_norm(x, r, w, 1e-6)
+        assert vllm_plugin.supports_rms_norm(x, w, 1e-6)
+        torch.ops.inference_performance_lab.fused_add_rms_norm(x, r, w, 1e-6)
+        torch.ops.inference_performance_lab.rms_norm(torch.empty_like(x), x, w, 1e-6)
+    a = torch.zeros(4, 8, dtype=torch.bfloat16)
+    assert vllm_plugin._share_memory(a, a) and not vllm_plugin._share_memory(a, a.clone())
