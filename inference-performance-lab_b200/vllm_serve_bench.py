@@ -3,7 +3,7 @@
 
     python inference-performance-lab_b200/vllm_serve_bench.py --provider inference_lab|vllm_c
         [--concurrency 1,8,32] [--num-prompts 64] [--input-len 2048] [--output-len 32]
-        [--profile] [--port 8011] [--workdir DIR]
+        [--custom-ops +silu_and_mul] [--profile] [--port 8011] [--workdir DIR]
 
 It follows the reference's scripts: scripts/serve.sh:10-41 (the provider chosen with
 VLLM_PLUGINS and --ir-op-priority; bf16, --max-model-len 4096, --gpu-memory-utilization 0.90,
@@ -22,7 +22,10 @@ keeps every prompt at exactly --input-len tokens).
 
 Providers: ``vllm_c`` = vLLM's own CUDA kernels, the reference's comparison arm
 (VLLM_PLUGINS=""); ``inference_lab`` = this library for fused_add_rms_norm and rms_norm (IR
-providers) and SiluAndMul (the second entry point). With --profile, a short extra run is traced
+providers, lowered into the compiled graph) and SiluAndMul (the second entry point). Under vLLM's
+default compilation custom ops are off and SiLU-and-mul is fused by Inductor into a Triton kernel
+for either provider; --custom-ops +silu_and_mul turns vLLM's SiluAndMul op on, which then runs
+this library's kernel (inference_lab) or vLLM's (vllm_c). With --profile, a short extra run is traced
 with vLLM's torch profiler and the norm and activation kernels are listed by name with launch
 counts and device time, which shows what ran inside the compiled, CUDA-graphed model.
 
