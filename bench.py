@@ -604,6 +604,7 @@ def measure_workload(name: str, spec, dist, device, stream, steps: int, warmup: 
     peak, peak_kind = load_peak()
     local_us = timing["local_ms"] / steps * 1e3
     total_bytes = step_bytes(spec, total_rows)
+    clock_summary = clocks.summary()
     result = {
         "workload": workload_name(spec),
         "metric": workload.metric(),
@@ -624,7 +625,10 @@ def measure_workload(name: str, spec, dist, device, stream, steps: int, warmup: 
         "launch": {k: timing[k] for k in ("host_us_per_call", "queued_before_start", "hold_us",
                                           "unqueued_us_per_step", "idle_us_per_step")},
         "parity": parity,
-        "clocks": clocks.summary(),
+        "clocks": clock_summary,
+        # Device time per step times the median SM clock under load: comparable across boxes
+        # whose clocks differ (cycles per step, in microsecond-megahertz).
+        "us_x_median_sm_mhz": (timing["us_per_step"] * clock_summary["sm_mhz"]) if clock_summary["sm_mhz"] else None,
         "_local_us": local_us,
         "_peak": (peak, peak_kind),
         "_calls": calls,
@@ -879,6 +883,7 @@ def run_ours(args, spec) -> None:
             "frac_of_same_traffic_torch_op": achieved / same_traffic["achieved"],
         },
         "launch": main["launch"],
+        "us_x_median_sm_mhz": main["us_x_median_sm_mhz"],
         "parity": {**main["parity"], "parity_ok_all_ranks": parity_ok},
         "cpu_baseline": cpu,
         "e2e": e2e,

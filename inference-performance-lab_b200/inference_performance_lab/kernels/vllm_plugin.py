@@ -164,3 +164,10 @@ def register_silu_and_mul() -> None:
             output = torch.empty(x.shape[:-1] + (x.shape[-1] // 2,), dtype=x.dtype, device=x.device)
             torch.ops.inference_performance_lab.silu_and_mul(output, x)
             return output
+
+    # The registry keys the replacement by the class it replaces ("SiluAndMul"), and registering
+    # renames it to that key; vLLM's switch for the op under compilation is its op name,
+    # `custom_ops: ["+silu_and_mul"]`, so give the replacement that name back: the same switch that
+    # turns vLLM's own SiLU kernel on (it is off by default under torch.compile, where Inductor
+    # fuses the native SiLU) turns this one on.
+    InferenceLabSiluAndMul.name = SiluAndMul.name

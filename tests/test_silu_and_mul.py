@@ -209,11 +209,17 @@ def test_vllm_silu_and_mul_layer_runs_the_b200_kernel() -> None:
 
     from inference_performance_lab.kernels import vllm_plugin
 
+    from vllm.config import CompilationConfig
+
     vllm_plugin.register_silu_and_mul()
     vllm_plugin.register_silu_and_mul()  # idempotent
     with set_current_vllm_config(VllmConfig()):
         layer = SiluAndMul()
     assert type(layer).__name__ == "InferenceLabSiluAndMul"
+    # vLLM's own switch for the op under compilation turns the replacement on.
+    assert type(layer).name == SiluAndMul.name == "silu_and_mul"
+    with set_current_vllm_config(VllmConfig(compilation_config=CompilationConfig(custom_ops=["+silu_and_mul"]))):
+        assert type(layer).enabled()
     torch.manual_seed(4)
     x = (torch.randn(128, 37888, device="cuda") * 2).to(torch.bfloat16)
     y = layer.forward_cuda(x)

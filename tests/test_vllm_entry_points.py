@@ -36,6 +36,7 @@ print(json.dumps({
     "fused_add_rms_norm": sorted(ir.ops.fused_add_rms_norm.impls),
     "rms_norm": sorted(ir.ops.rms_norm.impls),
     "oot": sorted(op_registry_oot),
+    "oot_op_name": op_registry_oot["SiluAndMul"].name,
     "schema": str(torch.ops.inference_performance_lab.fused_add_rms_norm.default._schema),
 }))
 """
@@ -72,6 +73,7 @@ def test_vllm_loads_the_providers_through_the_entry_points(tmp_path: Path) -> No
     assert Path(found["package"]).is_relative_to(site)
     assert "inference_lab" in found["fused_add_rms_norm"] and "inference_lab" in found["rms_norm"]
     assert "SiluAndMul" in found["oot"]
+    assert found["oot_op_name"] == "silu_and_mul"  # vLLM's custom-op switch for SiLU-and-mul applies
     assert found["schema"].startswith("inference_performance_lab::fused_add_rms_norm(Tensor(a!) x")
 
 
