@@ -186,3 +186,20 @@ def test_bench_control_plane_is_gloo_on_the_host() -> None:
     assert elapsed == 3.0
     assert verdict is False  # one rank's failed check fails the run
     assert [r["rank"] for r in per_rank] == [0, 1] and per_rank[1]["us"] == 11.0
+
+
+def test_row_sharded_batch_rejects_bad_arguments() -> None:
+    from inference_performance_lab.kernels.sharding import RowShardedBatch
+
+    x = torch.zeros(8, 16, dtype=torch.bfloat16)
+    w = torch.zeros(16, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="at least one device"):
+        RowShardedBatch(x, x.clone(), w, [])
+    with pytest.raises(ValueError, match="identical shapes"):
+        RowShardedBatch(x, torch.zeros(8, 8, dtype=torch.bfloat16), w, ["cuda:0"])
+    with pytest.raises(ValueError, match="final tensor dimension"):
+        RowShardedBatch(x, x.clone(), torch.zeros(8, dtype=torch.bfloat16), ["cuda:0"])
+    with pytest.raises(ValueError, match="bfloat16"):
+        RowShardedBatch(x.float(), x.float(), w, ["cuda:0"])
+    with pytest.raises(ValueError, match="not a CUDA device"):
+        RowShardedBatch(x, x.clone(), w, ["cpu"])

@@ -1,12 +1,16 @@
-"""Row sharding on GPUs: every rank runs its own block of rows through the CUDA kernel on its own
-device and checks it against the oracle, with no peer memory and no collective on the data path.
+"""Row sharding on GPUs: every block of rows runs through the CUDA kernel on its own device and is
+checked against the oracle, with no peer memory and no collective on the data path.
 
-Two ranks (one process per GPU, spawned), a gloo group for the verdicts only. The batch is a
-[4099, 8192] slice of the row-sharded workload's recipe (eps 1e-5, each rank's rows generated on
-its own device from seed + rank, the same weight on every device): an odd row count, so the two
-blocks differ by one row. Each rank checks its first and last row and a spread sample against the
-C oracle - residual bit for bit, output within rtol = atol = 1e-2 and one bf16 ulp - and the
-gathered blocks must tile the batch. Needs two GPUs; skipped on fewer.
+* One process per GPU: two ranks (spawned), a gloo group for the verdicts only. The batch is a
+  [4099, 8192] slice of the row-sharded workload's recipe (eps 1e-5, each rank's rows generated on
+  its own device from seed + rank, the same weight on every device): an odd row count, so the two
+  blocks differ by one row. Each rank checks its first and last row and a spread sample against
+  the C oracle - residual bit for bit, output within rtol = atol = 1e-2 and one bf16 ulp - and the
+  gathered blocks must tile the batch. Needs two GPUs; skipped on fewer.
+* One process for several devices (``RowShardedBatch``): a [4099, 8192] host batch split into
+  blocks, one stream and weight replica per block, enqueued from one thread and gathered back;
+  every row is checked. Three blocks on one GPU's separate streams always run; two GPUs when
+  present.
 """
 
 from __future__ import annotations
@@ -100,3 +104,42 @@ def test_each_rank_runs_its_shard_on_its_own_gpu() -> None:
     for g in gathered:
         assert g["ok"], g
         assert g["fault"] == 0 and g["rows_checked"] >= 64 and g["kernel"].startswith("rmsnorm_stash_kernel")
+
+
+def _check_batch(devices) -> None:
+    from inference_performance_lab.kernels.sharding import RowShardedBatch
+    from oracle import oracle
+
+    from parity import assert_bits_equal, assert_close_to_oracle
+
+    rows, hidden = 4099, 8192
+    generator = torch.Generator().manual_seed(11)
+    x = torch.randn(rows, hidden, generator=generator).to(torch.bfloat16).pin_memory()
+    r = torch.randn(rows, hidden, generator=generator).to(torch.bfloat16).pin_memory()
+    w = (torch.randn(hidden, generator=generator) * 0.1 + 1).to(torch.bfloat16)
+    want_out, want_res = oracle.c_fused_add_rms_norm(oracle.tensor_bits(x), oracle.tensor_bits(r),
+                                                     oracle.tensor_bits(w), EPS)
+    batch = RowShardedBatch(x, r, w, devices)
+    shards = [shard for shard, _, _ in batch.blocks]
+    assert shards[0].start == 0 and shards[-1].stop == rows
+    assert [b.device.index for b in batch._blocks] == [torch.device("cuda", d).index for d in devices]
+    batch.fused_add_rms_norm(EPS)
+    got_x, got_r = batch.gather()
+    assert_bits_equal(got_r, want_res, f"residual over {devices}")
+    assert_close_to_oracle(got_x, want_out, f"output over {devices}")
+
+
+def test_row_sharded_batch_blocks_on_separate_streams_of_one_gpu() -> None:
+    """Three row blocks of one host batch on GPU 0, each on its own stream with its own weight
+    replica, enqueued from one thread; gathered in row order, every row matches the oracle."""
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test run without a CUDA device")
+    _check_batch([0, 0, 0])
+
+
+def test_row_sharded_batch_over_two_gpus() -> None:
+    """The same batch split over two GPUs from one process: each device runs its block on its own
+    stream, nothing crosses between devices, and the gathered rows match the oracle."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip(f"needs 2 GPUs, found {torch.cuda.device_count()}")
+    _check_batch([0, 1])
