@@ -815,7 +815,13 @@ def run_ours(args, spec) -> None:
                                         "parity_ok": rec["parity"]["parity_ok"]})
                 rec["per_rank"] = per_rank
                 traffic = load_traffic(name)
-                rec["traffic"] = traffic
+                if traffic is not None:
+                    scaled = traffic["bytes_per_launch"] * rec["rows_per_rank"] / traffic["rows"]
+                    rec["traffic"] = {"bytes_per_launch": scaled,
+                                      "ratio": scaled / rec["bytes_per_step_per_rank"],
+                                      "source": traffic["command"]}
+                else:
+                    rec["traffic"] = None
                 subrecords[key] = public(rec)
                 del rec
                 torch.cuda.empty_cache()

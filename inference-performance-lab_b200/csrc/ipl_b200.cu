@@ -321,7 +321,7 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
         plan.chunks_per_lane = per_lane;
         plan.capped = long_rows && mode != kModePlain && hidden <= kStashCappedMaxHidden && rows > kCtaRowMaxRows;
         plan.threads = static_cast<unsigned>(threads);
-        plan.smem = 0;
+        plan.smem = per_lane == kStashChunks ? static_cast<size_t>(hidden) * 2u : 0;  // staged gamma
         plan.grid = static_cast<unsigned>(rows < INT_MAX ? rows : INT_MAX);
         // Registers a thread may take under each instance's launch bound: 64, the capped
         // instance 96, eight chunks a thread with a residual 128.
@@ -405,7 +405,8 @@ const char* mode_label(int mode) {
     return mode == kModeFused ? "fused RMSNorm" : mode == kModePlain ? "RMSNorm" : "fused RMSNorm fp8";
 }
 
-// The stash kernel uses no dynamic shared memory: each instance launches as planned.
+// The stash kernel's four-chunk instances stage gamma in plan.smem bytes of dynamic shared
+// memory (H * 2, at most 32 KB: under the default limit, no opt-in); the eight-chunk ones use none.
 template <int kMode>
 ipl_status launch_stash(const RmsPlan& plan, cudaStream_t stream, const WarpRowParams& w) {
     cudaError_t err;
@@ -420,7 +421,7 @@ ipl_status launch_stash(const RmsPlan& plan, cudaStream_t stream, const WarpRowP
     }
     err = plan.chunks_per_lane == kStashWideChunks
               ? launch(rmsnorm_stash_kernel<kStashWideChunks, kMode>, plan.grid, plan.threads, 0, stream, w)
-              : launch(rmsnorm_stash_kernel<kStashChunks, kMode>, plan.grid, plan.threads, 0, stream, w);
+              : launch(rmsnorm_stash_kernel<kStashChunks, kMode>, plan.grid, plan.threads, plan.smem, stream, w);
     if (err != cudaSuccess) {
         return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
     }

@@ -277,6 +277,16 @@ __device__ __forceinline__ bool spin_until_at_least(const int* counter, int targ
     }
 }
 
+// Asynchronous 16-byte copy global -> shared memory of this CTA (cp.async, allocating in L1, so
+// the SM's other CTAs reading the same source hit L1); completion by cp_async_wait_all. dst and
+// src 16-byte aligned. The copied bytes occupy no registers while in flight.
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+// Waits until every cp.async this thread issued has landed (visible to this thread; a barrier
+// after it makes them visible to the CTA).
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Bulk copy global -> shared (this CTA), completion counted on `bar` in bytes.
 // dst, src 16-byte aligned; bytes a multiple of 16. The L2 policy hint marks the source lines
 // evict-first: every byte is read exactly once.
