@@ -129,7 +129,7 @@ class RowShardedBatch:
         import torch
 
         x = torch.empty(self.rows, self.hidden, dtype=torch.bfloat16, pin_memory=True)
-        residual = torch.empty_like(x, pin_memory=True)
+        residual = torch.empty(self.rows, self.hidden, dtype=torch.bfloat16, pin_memory=True)
         for b in self._blocks:
             with torch.cuda.device(b.device), torch.cuda.stream(b.stream):
                 x[b.shard.start:b.shard.stop].copy_(b.x, non_blocking=True)
