@@ -992,7 +992,7 @@ def run_e2e(args, spec, workload, rows: int, batches, shared, stream, dist) -> d
             freed[k % 2].record(download)
         return freed[(n - 1) % 2]
 
-    pipeline(min(3, steps)).synchronize()
+    pipeline(max(3, args.warmup)).synchronize()  # W untimed steps, as every timed region has
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
