@@ -53,6 +53,9 @@ def build(reference: Path) -> Path:
     missing = [s for s in SOURCES if not (reference / s).is_file()]
     if missing:
         raise FileNotFoundError(f"reference sources not found under {reference}: {missing}")
+    inputs = [reference / s for s in SOURCES] + list(OVERLAY.rglob("*.h")) + [Path(__file__)]
+    if LIBRARY.exists() and LIBRARY.stat().st_mtime > max(p.stat().st_mtime for p in inputs):
+        return LIBRARY
     torch_root = Path(torch.__file__).resolve().parent
     cuda_home = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
     nvcc = cuda_home / "bin" / "nvcc"
