@@ -729,10 +729,10 @@ def run_reference(args, spec) -> None:
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    # Size each step's sample so that warm-up + K steps end within about a minute.
+    # Size each step's sample so that warm-up + K steps end within the budget (a minute by default).
     probe = cpu_reference_rate(spec, 0.5, sample_rows=min(spec["rows"], 256))
     per_row = probe["ms_per_call"] / 1e3 / min(spec["rows"], 256)
-    budget = 60.0 / max(args.steps + args.warmup, 1)
+    budget = args.reference_seconds / max(args.steps + args.warmup, 1)
     rows = int(max(1, min(spec["rows"], budget / per_row)))
     workload = OpWorkload(spec)
     call = workload.cpu_call(rows)
@@ -1055,6 +1055,8 @@ def main() -> None:
     parser.add_argument("--e2e-steps", type=int, default=200)
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--reference-seconds", type=float, default=60.0,
+                        help="--impl reference: CPU time budget of warm-up + timed steps")
     parser.add_argument("--no-subrecords", action="store_true",
                         help="measure the chosen workload only (no sharded / misaligned / silu records)")
     parser.add_argument("--rows", type=int, default=None,

@@ -92,3 +92,21 @@ def test_our_arm_prints_the_full_contract_line_on_a_gpu() -> None:
         assert sub["parity"]["parity_ok"] and sub["parity"]["parity_ok_all_ranks"], (key, sub["parity"])
         assert sub["value"] > 0 and 0.1 < sub["roofline_frac"] < 1.3 and sub["launch"]["queued_before_start"]
     assert d["sharded"]["rows_per_rank"] == 262144 and d["sharded"]["parity"]["rows_checked"] >= 64
+
+
+@pytest.mark.gpu
+def test_reference_arm_times_the_reference_kernels_on_this_gpu() -> None:
+    """The reference arm on a B200: its CPU line, plus the reference's own kernels compiled for
+    sm_100a timed on the four workloads and checked against the oracle (when they were built)."""
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test run without a CUDA device")
+    out = run_bench("--impl", "reference", "--steps", "5", "--warmup", "3", "--reference-seconds", "2")
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads([line for line in out.stdout.splitlines() if line.strip()][-1])
+    assert d["impl"] == "reference" and d["value"] > 0
+    kernels = d.get("reference_cuda_kernels")
+    if kernels is None or "unavailable" in kernels:
+        pytest.skip(f"the reference's kernels were not built: {kernels}")
+    for key in ("rmsnorm", "misaligned", "sharded", "silu"):
+        assert kernels[key]["parity"]["parity_ok"], (key, kernels[key]["parity"])
+        assert kernels[key]["value"] > 0
