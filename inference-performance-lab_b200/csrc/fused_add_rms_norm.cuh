@@ -541,6 +541,9 @@ struct WarpRowParams {
     // for the row one wave ahead of theirs. See prefetch_next_wave_row.
     int64_t lookahead;
     int64_t lookahead_ctas;
+    // Cluster kernel: 16-byte chunks of a row that each CTA of a cluster owns (the last CTA
+    // may own fewer).
+    int cluster_slice;
 };
 
 template <int kChunks, int kMode>
@@ -909,6 +912,133 @@ __global__ void __launch_bounds__(kCapped ? kStashCappedThreads : kStashMaxThrea
                 } else {
                     st_v4(p.out + row * p.hidden + 8 * c, chunk_to_bf16(v));
                 }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// A row split over a thread-block cluster (H % 8 == 0, 16-byte aligned rows): the C CTAs of a
+// cluster (2..8, along x; grid = rows * C) share one row, CTA k owning its 16-byte chunks
+// [k * S, min((k + 1) * S, H / 8)), S = p.cluster_slice, in registers as in the stash kernel
+// (kUnroll chunks a thread, gamma staged in shared memory by cp.async). Each CTA reduces its Σv²
+// over its warps through shared memory, then writes it into slot k of every CTA's `row_sums`
+// through distributed shared memory; after one cluster barrier every CTA adds the C slots in the
+// same order, so all of them normalise with the same inverse RMS. Two places where one CTA a
+// row leaves the GPU short of work: rows longer than one CTA holds in registers (H > 32768, where
+// the only other aligned kernel is the rowwise one with 2-byte accesses), and launches of a few
+// long rows, where C CTAs a row put C times the SMs on the row's loads.
+//
+// Barrier protocol, per cluster: every thread arrives (relaxed) at the start and waits before its
+// CTA's remote stores, so every CTA of the cluster is running before any writes into its shared
+// memory; the stores are followed by a release arrive and an acquire wait, after which each CTA
+// reads only its own shared memory, so a CTA that finishes early leaves while no peer can still
+// access its shared memory. Both are hardware cluster barriers (no spin of ours), reached
+// unconditionally by every thread.
+constexpr int kClusterMaxCtas = 8;  // the portable cluster size: no opt-in attribute
+
+template <int kUnroll, int kMode>
+__global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_cluster_kernel(const WarpRowParams p) {
+    constexpr bool kResidual = kMode != kModePlain;
+    constexpr bool kFp8 = kMode == kModeFusedFp8;
+    __shared__ float partials[kStashMaxThreads / kWarpSize];
+    __shared__ float row_sums[kClusterMaxCtas];
+    extern __shared__ __align__(16) unsigned char gamma_smem[];  // this CTA's slice of gamma
+    const int threads = static_cast<int>(blockDim.x);
+    const int warps = threads / kWarpSize;
+    const int warp = threadIdx.x / kWarpSize;
+    const int lane = threadIdx.x % kWarpSize;
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t ctas = cluster_nctarank();
+    const int64_t row = static_cast<int64_t>(blockIdx.x) / ctas;
+    const int chunks = p.hidden >> 3;
+    const int first = static_cast<int>(rank) * p.cluster_slice;
+    const int end = first + p.cluster_slice < chunks ? first + p.cluster_slice : chunks;
+    const float hidden_f = static_cast<float>(p.hidden);
+    const bool weight_aligned = (reinterpret_cast<uintptr_t>(p.weight) & 15u) == 0;
+    const uint32_t gamma_base = smem_addr(gamma_smem);
+    const uint16_t* xr = p.x + row * p.hidden;
+    uint16_t* rr = kResidual ? p.residual + row * p.hidden : nullptr;
+
+    cluster_arrive_relaxed();
+    if (threadIdx.x == 0 && end > first) {  // this CTA's slice into L2 while the previous kernel drains
+        const uint32_t bytes = 16u * static_cast<uint32_t>(end - first);
+        bulk_prefetch_l2(xr + 8 * first, bytes);
+        if constexpr (kResidual) bulk_prefetch_l2(rr + 8 * first, bytes);
+        if (blockIdx.x < kGammaPrefetchCtas) prefetch_span_l2(p.weight + 8 * first, bytes);
+    }
+    grid_dependency_wait();
+    grid_launch_dependents();
+    if (weight_aligned) {
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int c = first + static_cast<int>(threadIdx.x) + u * threads;
+            if (c < end) cp_async_16(gamma_base + 16u * (c - first), p.weight + 8 * c);
+        }
+    }
+    const float scale_inv = kFp8 ? 1.0f / *p.scale : 1.0f;
+    const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
+
+    U32x4 xs[kUnroll], rs[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+        const int c = first + static_cast<int>(threadIdx.x) + u * threads;
+        if (c < end) {
+            xs[u] = ld_v4(xr + 8 * c);
+            if constexpr (kResidual) rs[u] = ld_v4(rr + 8 * c);
+        }
+    }
+    F32x2 acc = f32x2_make(0.0f, 0.0f);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+        const int c = first + static_cast<int>(threadIdx.x) + u * threads;
+        if (c < end) {
+            Pairs4 v;
+            if constexpr (kResidual) {
+                v = chunk_sum(xs[u], rs[u]);
+                st_v4(rr + 8 * c, chunk_to_bf16(v));
+            } else {
+                v = chunk_widen(xs[u]);
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc = f32x2_fma(v.v[e], v.v[e], acc);
+        }
+    }
+    float acc_lo, acc_hi;
+    f32x2_split(acc, acc_lo, acc_hi);
+    const float warp_total = warp_sum(acc_lo + acc_hi);
+    if (lane == 0) partials[warp] = warp_total;
+    __syncthreads();
+    float cta_total = 0.0f;
+    for (int w = 0; w < warps; ++w) cta_total += partials[w];
+    cluster_wait_acquire();  // every CTA of the cluster is running
+    if (threadIdx.x < ctas) {
+        st_shared_cluster_f32(map_shared_to_rank(smem_addr(&row_sums[rank]), threadIdx.x), cta_total);
+    }
+    if (weight_aligned) cp_async_wait_all();
+    cluster_arrive_release();
+    cluster_wait_acquire();  // every CTA's sum is in row_sums
+    float sumsq = 0.0f;
+    for (uint32_t k = 0; k < ctas; ++k) sumsq += row_sums[k];
+    const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
+    const F32x2 inv2 = f32x2_make(inv, inv);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+        const int c = first + static_cast<int>(threadIdx.x) + u * threads;
+        if (c < end) {
+            Pairs4 v = kResidual ? chunk_sum(xs[u], rs[u]) : chunk_widen(xs[u]);
+            const Pairs4 w = chunk_widen(weight_aligned ? lds_v4(gamma_base + 16u * (c - first))
+                                                        : load_weight_chunk(p.weight, c, false));
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v.v[e] = f32x2_mul(f32x2_mul(v.v[e], inv2), w.v[e]);
+            if constexpr (kFp8) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) v.v[e] = f32x2_mul(v.v[e], scale_inv2);
+                const uint32_t w0 = f32x2_to_e4m3x2(v.v[0]) | (f32x2_to_e4m3x2(v.v[1]) << 16);
+                const uint32_t w1 = f32x2_to_e4m3x2(v.v[2]) | (f32x2_to_e4m3x2(v.v[3]) << 16);
+                st_v2(p.out8 + row * p.hidden + 8 * c, w0, w1);
+            } else {
+                st_v4(p.out + row * p.hidden + 8 * c, chunk_to_bf16(v));
             }
         }
     }

@@ -98,10 +98,31 @@ cudaError_t launch(Kernel kernel, unsigned grid, unsigned block, size_t smem, cu
     return cudaLaunchKernelEx(&config, kernel, args...);
 }
 
+// The same with the grid in thread-block clusters of `cluster` CTAs along x (grid a multiple of it).
+template <typename Kernel, typename... Args>
+cudaError_t launch_clustered(Kernel kernel, unsigned grid, unsigned cluster, unsigned block, size_t smem,
+                             cudaStream_t stream, Args... args) {
+    cudaLaunchAttribute attribute[2];
+    attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[0].val.programmaticStreamSerializationAllowed = 1;
+    attribute[1].id = cudaLaunchAttributeClusterDimension;
+    attribute[1].val.clusterDim.x = cluster;
+    attribute[1].val.clusterDim.y = 1;
+    attribute[1].val.clusterDim.z = 1;
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(grid);
+    config.blockDim = dim3(block);
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    config.attrs = attribute;
+    config.numAttrs = 2;
+    return cudaLaunchKernelEx(&config, kernel, args...);
+}
+
 // ------------------------------------------------------------------------------------------
 // add + RMSNorm / RMSNorm planning
 
-enum class RmsFamily { kNone, kStaged, kWarpRow, kCtaRow, kStash, kShifted, kRowwiseCached, kRowwiseTwoPass };
+enum class RmsFamily { kNone, kStaged, kWarpRow, kCtaRow, kStash, kShifted, kCluster, kRowwiseCached, kRowwiseTwoPass };
 
 struct RmsPlan {
     RmsFamily family = RmsFamily::kNone;
@@ -112,6 +133,8 @@ struct RmsPlan {
     int phase = 0;            // shifted kernel: elements from the 16-byte block to each row
     int64_t lookahead = 0;       // stash and shifted kernels: one resident wave, when rows exceed it
     int64_t lookahead_ctas = 0;  // ... and how many CTAs look one wave ahead
+    int cluster = 0;             // cluster kernel: CTAs a row (2..8) ...
+    int cluster_slice = 0;       // ... and the 16-byte chunks each owns
     unsigned grid = 0;
     size_t smem = 0;
     StagedParams staged = {};
@@ -136,6 +159,10 @@ const char* rms_kernel_name(const RmsPlan& plan, int mode) {
                                                "rmsnorm_stash_kernel<4, fp8>"};
     static const char* const kStashWideNames[3] = {"rmsnorm_stash_kernel<8>", "rmsnorm_stash_kernel<8, plain>",
                                                    "rmsnorm_stash_kernel<8, fp8>"};
+    static const char* const kClusterNames[3][3] = {
+        {"rmsnorm_cluster_kernel<1>", "rmsnorm_cluster_kernel<2>", "rmsnorm_cluster_kernel<4>"},
+        {"rmsnorm_cluster_kernel<1, plain>", "rmsnorm_cluster_kernel<2, plain>", "rmsnorm_cluster_kernel<4, plain>"},
+        {"rmsnorm_cluster_kernel<1, fp8>", "rmsnorm_cluster_kernel<2, fp8>", "rmsnorm_cluster_kernel<4, fp8>"}};
     static const char* const kRowwiseNames[3][2] = {
         {"rmsnorm_rowwise_kernel<cached>", "rmsnorm_rowwise_kernel<two-pass>"},
         {"rmsnorm_rowwise_kernel<cached, plain>", "rmsnorm_rowwise_kernel<two-pass, plain>"},
@@ -168,6 +195,9 @@ const char* rms_kernel_name(const RmsPlan& plan, int mode) {
                  "rmsnorm_shifted_kernel<7, plain>"}};
             return mode == kModeFusedFp8 ? "invalid" : kShiftedNames[mode][plan.phase - 1];
         }
+        case RmsFamily::kCluster:
+            while ((1 << i) < plan.chunks_per_lane) ++i;
+            return kClusterNames[mode][i];
         case RmsFamily::kRowwiseCached: return kRowwiseNames[mode][0];
         case RmsFamily::kRowwiseTwoPass: return kRowwiseNames[mode][1];
     }
@@ -213,6 +243,60 @@ void set_lookahead(RmsPlan& plan, int64_t rows, int64_t wave) {
     plan.lookahead_ctas = rows > wave ? (rows <= kLookaheadAllWaves * wave ? rows : wave) : 0;
 }
 
+// The cluster kernel with `ctas` CTAs a row: each owns ceil(H / 8 / ctas) 16-byte chunks and
+// stages its slice of gamma. Chunks a thread (1, 2 or 4): the most that leave the CTA at least
+// 128 threads, more where 512 threads would not hold the slice. Measured against fewer chunks a
+// thread over more threads: 512 x 65536 48.1 against 67.4 us, 2048 x 49152 -10 %.
+void set_cluster(RmsPlan& plan, int64_t rows, int64_t hidden, int ctas) {
+    const int64_t slice = (hidden / 8 + ctas - 1) / ctas;
+    int per_thread = 1;
+    while (per_thread < kStashChunks && (slice + 2 * per_thread - 1) / (2 * per_thread) >= 128) per_thread *= 2;
+    while (per_thread < kStashChunks && (slice + per_thread - 1) / per_thread > kStashMaxThreads) per_thread *= 2;
+    plan.family = RmsFamily::kCluster;
+    plan.chunks_per_lane = per_thread;
+    const int64_t threads = (slice + plan.chunks_per_lane - 1) / plan.chunks_per_lane;
+    plan.threads = static_cast<unsigned>((threads + kWarpSize - 1) / kWarpSize * kWarpSize);
+    plan.cluster = ctas;
+    plan.cluster_slice = static_cast<int>(slice);
+    plan.smem = static_cast<size_t>(slice) * 16u;
+    plan.grid = static_cast<unsigned>(rows * ctas);
+}
+
+// CTAs a row for the cluster kernel (aligned rows, H % 8 == 0), or 0 where one CTA a row plans
+// better. From cold-L2 sweeps on B200 (CUDA graph, add+RMSNorm and RMSNorm, 1-2048 rows x H
+// 6144-131072, cluster sizes 2, 4 and 8 against the kernels planned before):
+// * H > 32768 (up to 131072, 512 threads of four chunks in each of 8 CTAs): always, 8 CTAs a row.
+//   The only other aligned kernel there is the rowwise one (2-byte accesses, the row read twice):
+//   2.8-4.3x faster from 512 rows (512 x 65536 48.4 against 208 us), 9-45x for 1-64 rows;
+//   8 CTAs were 1-12 % ahead of 4 at every size;
+// * few long rows, where one CTA a row leaves SMs idle and each CTA's row takes long to load:
+//   16384 < H <= 32768 up to 256 rows (RMSNorm 128): 1.06-2.2x against the stash kernel's
+//   eight-chunk instance (8 x 32768 2.70 against 5.80 us); 8192 <= H <= 16384 up to 32 rows,
+//   6144 <= H < 8192 up to 16: 1.04-1.56x against the CTA-per-row kernel (1 x 16384 2.10 against
+//   3.28 us); H >= 12288 and more rows than SMs up to 256, where the CTA-per-row kernel needs a
+//   second wave: 1.09-1.33x. Outside these ranges the cluster was level or up to 30 % slower;
+// * cluster size: 8 CTAs for up to 16 rows; otherwise the most (8, 4, 2) that leave each CTA at
+//   least 256 chunks and the launch at most 768 CTAs - the GPU starts CTAs at about one a
+//   nanosecond, and a CTA of one chunk a thread costs more to start than it saves (192 x 16384:
+//   4 CTAs a row 5.71 us, 8 CTAs 7.33).
+int cluster_ctas_for(int64_t rows, int64_t hidden, int mode, int sm_count) {
+    const int64_t chunks = hidden / 8;
+    if (hidden > kStashMaxLongHidden) {
+        const bool fits = chunks <= static_cast<int64_t>(kClusterMaxCtas) * kStashMaxThreads * kStashChunks;
+        return fits && rows <= INT_MAX / kClusterMaxCtas ? kClusterMaxCtas : 0;
+    }
+    if (hidden < 6144) return 0;
+    const bool use = hidden > kStashMaxHidden
+                         ? rows <= (mode == kModePlain ? 128 : 256)
+                         : rows <= (hidden >= 8192 ? 32 : 16) ||
+                               (hidden >= 12288 && rows > sm_count && rows <= kCtaRowMaxRows);
+    if (!use) return 0;
+    if (rows <= 16) return kClusterMaxCtas;
+    int ctas = kClusterMaxCtas;
+    while (ctas > 2 && (chunks / ctas < 256 || rows * ctas > 768)) ctas /= 2;
+    return ctas;
+}
+
 // Pure function of the arguments and two device limits. `other` is the residual (fused modes) or
 // the output (plain mode); either must share x's offset modulo 16 bytes for the staged kernel.
 // `out8` is the fp8 output of kModeFusedFp8, whose vector paths need 16-byte aligned rows
@@ -234,6 +318,14 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
     int max_stages = room > 0 ? static_cast<int>(room / (stage_bytes + 2 * 8)) : 0;
     if (max_stages > kStagedMaxStages) max_stages = kStagedMaxStages;
 
+    // Rows split over a thread-block cluster (cluster_ctas_for).
+    if (hidden % 8 == 0 && ((xa | oa) & 15u) == 0 && fp8_vector_ok) {
+        const int ctas = cluster_ctas_for(rows, hidden, mode, sm_count);
+        if (ctas > 0) {
+            set_cluster(plan, rows, hidden, ctas);
+            return plan;
+        }
+    }
     // Aligned rows (H % 8 == 0, 16-byte aligned, H <= 16384) have four kernels. The choice, from
     // cold-L2 sweeps on B200 against each other and vLLM's kernels (1..262144 rows, H 128..16384):
     // * up to 256 rows (decode batches), or with one chunk a thread (H <= 4096) as many rows as
@@ -398,6 +490,7 @@ WarpRowParams row_params(const RmsPlan& plan) {
     w.epsilon = plan.staged.epsilon;
     w.lookahead = plan.lookahead;
     w.lookahead_ctas = plan.lookahead_ctas;
+    w.cluster_slice = plan.cluster_slice;
     return w;
 }
 
@@ -532,6 +625,20 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8
                 }
                 return IPL_SUCCESS;
             }
+        }
+        case RmsFamily::kCluster: {
+            const WarpRowParams w = row_params(plan);
+            const unsigned cluster = static_cast<unsigned>(plan.cluster);
+            cudaError_t err = cudaSuccess;
+            switch (plan.chunks_per_lane) {
+                case 1: err = launch_clustered(rmsnorm_cluster_kernel<1, kMode>, plan.grid, cluster, plan.threads, plan.smem, stream, w); break;
+                case 2: err = launch_clustered(rmsnorm_cluster_kernel<2, kMode>, plan.grid, cluster, plan.threads, plan.smem, stream, w); break;
+                default: err = launch_clustered(rmsnorm_cluster_kernel<4, kMode>, plan.grid, cluster, plan.threads, plan.smem, stream, w); break;
+            }
+            if (err != cudaSuccess) {
+                return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
+            }
+            return IPL_SUCCESS;
         }
         case RmsFamily::kRowwiseCached:
         case RmsFamily::kRowwiseTwoPass: {

@@ -345,6 +345,40 @@ __device__ __forceinline__ void grid_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---- thread-block clusters and distributed shared memory -----------------------------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t rank;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    return rank;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+    uint32_t n;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(n));
+    return n;
+}
+// The cluster barrier is a hardware barrier over every thread of every CTA of the cluster, whose
+// CTAs the GPU schedules together: it completes once all of them have arrived, with no spin of
+// ours. Each thread must reach every arrive and wait (`.aligned`: whole warps, converged).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The shared::cluster address of CTA `rank`'s copy of the variable at this CTA's `addr`.
+__device__ __forceinline__ uint32_t map_shared_to_rank(uint32_t addr, uint32_t rank) {
+    uint32_t mapped;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(mapped) : "r"(addr), "r"(rank));
+    return mapped;
+}
+__device__ __forceinline__ void st_shared_cluster_f32(uint32_t addr, float value) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(value) : "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float value) {
 #pragma unroll
     for (int offset = kWarpSize / 2; offset > 0; offset >>= 1) {

@@ -132,7 +132,7 @@ def test_plain_rms_in_place_is_accepted_by_the_plan() -> None:
     # Each stash thread reads its chunks into registers before it writes them, so in place is safe.
     assert capi.rms_norm_plan(BASE, BASE, BASE + 8192, 2048, 3584) == "rmsnorm_stash_kernel<4, plain>"
     assert capi.rms_norm_plan(BASE + 2, BASE, BASE + 8192, 8, 3584) == "rmsnorm_rowwise_kernel<cached, plain>"
-    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 1, 8192) == "rmsnorm_cta_kernel<2, plain>"
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 64, 8192) == "rmsnorm_cta_kernel<2, plain>"
     # Rows of 8192+ elements, 4096+ of them: eight chunks a thread.
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 4095, 8192) == "rmsnorm_stash_kernel<4, plain>"
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 8192, 8192) == "rmsnorm_stash_kernel<8, plain>"
@@ -160,8 +160,11 @@ def test_fp8_quant_arguments_and_plans() -> None:
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 16384) == "rmsnorm_stash_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 18432) == "rmsnorm_stash_kernel<8, fp8, capped>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 32768) == "rmsnorm_stash_kernel<8, fp8>"
+    # Longer aligned rows: the cluster kernel, eight CTAs a row, up to H = 131072.
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 32776) == "rmsnorm_cluster_kernel<4, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 8, 32768) == "rmsnorm_cluster_kernel<4, fp8>"
     # The fp8 output has no staged plan: rows it cannot vectorise go to the row kernel.
-    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 32776).startswith("rmsnorm_rowwise_kernel")
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 131080).startswith("rmsnorm_rowwise_kernel")
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 100000, 1024) == "rmsnorm_stash_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 100000, 896) == "rmsnorm_warp_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 1024) == "rmsnorm_stash_kernel<4, fp8>"
@@ -238,7 +241,7 @@ def test_rms_plan_selection() -> None:
     assert rms_plan(0, 0, 1, 8, 3584) == "rmsnorm_cta_kernel<1>"
     assert rms_plan(0, 0, 0, 1, 3584) == "rmsnorm_cta_kernel<1>"
     assert rms_plan(0, 0, 0, 256, 8192) == "rmsnorm_cta_kernel<2>"
-    assert rms_plan(0, 0, 0, 5, 16384) == "rmsnorm_cta_kernel<4>"
+    assert rms_plan(0, 0, 0, 100, 16384) == "rmsnorm_cta_kernel<4>"
     assert rms_plan(0, 0, 0, 5, 2048) == "rmsnorm_cta_kernel<1>"
     assert rms_plan(0, 0, 0, 64, 2056) == "rmsnorm_cta_kernel<1>"
     # One chunk a thread (H <= 4096): the CTA per row also while every row's CTA is resident at once
@@ -270,13 +273,14 @@ def test_rms_plan_selection() -> None:
     assert rms_plan(0, 0, 0, 1000, 16392) == "rmsnorm_stash_kernel<8, capped>"
     assert rms_plan(0, 0, 0, 8192, 18432) == "rmsnorm_stash_kernel<8, capped>"
     assert rms_plan(0, 0, 0, 257, 20480) == "rmsnorm_stash_kernel<8, capped>"
-    assert rms_plan(0, 0, 0, 256, 18432) == "rmsnorm_stash_kernel<8>"
+    assert rms_plan(0, 0, 0, 257, 18432) == "rmsnorm_stash_kernel<8, capped>"
     assert rms_plan(0, 0, 0, 8192, 20488) == "rmsnorm_stash_kernel<8>"
     assert rms_plan(0, 0, 0, 8192, 32768) == "rmsnorm_stash_kernel<8>"
     assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 8192, 18432) == "rmsnorm_stash_kernel<8, plain>"
-    # Longer rows, or rows off 16 bytes too long for the CTA kernels: the staged ring while two
-    # stages fit, else the two-pass row kernel.
-    assert rms_plan(0, 0, 0, 1000, 32776) == "rmsnorm_rowwise_kernel<two-pass>"
+    # Longer aligned rows: the cluster kernel (test_cluster_plan_selection); rows off 16 bytes too
+    # long for the CTA kernels: the staged ring while two stages fit, else the two-pass row kernel.
+    assert rms_plan(0, 0, 0, 1000, 32776) == "rmsnorm_cluster_kernel<4>"
+    assert rms_plan(0, 0, 0, 1000, 131080) == "rmsnorm_rowwise_kernel<two-pass>"
     assert rms_plan(1, 1, 0, 1000, 16392).startswith("rmsnorm_staged_kernel")
     # Short aligned rows: a CTA per row while the CTAs are resident at once; beyond that a warp per
     # row (eight rows a CTA) for rows that move under 7 KiB, the stash kernel for longer ones.
@@ -300,15 +304,53 @@ def test_rms_plan_selection() -> None:
         for rows in (300, 1000, 100000):
             assert rms_plan(0, 0, 0, rows, hidden).startswith(("rmsnorm_staged_kernel", "rmsnorm_rowwise_kernel"))
             assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, rows, hidden) != "invalid"
-    # Rows too long for two stages fall back to the two-pass row kernel.
-    assert rms_plan(0, 0, 0, 64, 40000) == "rmsnorm_rowwise_kernel<two-pass>"
+    # Rows too long for two stages fall back to the two-pass row kernel (aligned ones of H % 8 == 0
+    # to the cluster kernel).
+    assert rms_plan(0, 0, 0, 64, 40002) == "rmsnorm_rowwise_kernel<two-pass>"
     assert rms_plan(1, 0, 0, 64, 40000) == "rmsnorm_rowwise_kernel<two-pass>"
+    assert rms_plan(0, 0, 0, 64, 40000) == "rmsnorm_cluster_kernel<4>"
     assert rms_plan(0, 0, 0, 0, 3584) == "none"
     assert rms_plan(0, 0, 0, 4, 0) == "invalid"
 
 
 def silu_plan(out_off: int, in_off: int, rows: int, inter: int) -> str:
     return capi.silu_and_mul_plan(BASE + 2 * out_off, BASE + (1 << 34) + 2 * in_off, rows, inter)
+
+
+def test_cluster_plan_selection() -> None:
+    """Rows split over a thread-block cluster: aligned rows longer than 32768 elements always, few
+    long rows where one CTA a row leaves SMs idle; the kernel name carries the chunks a thread
+    (the most that leave each CTA 128+ threads)."""
+    plain = lambda rows, hidden: capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, rows, hidden)
+    # H > 32768: eight CTAs a row at any row count (512 threads of four chunks at H = 131072).
+    for rows in (1, 64, 2048, 262144):
+        assert rms_plan(0, 0, 0, rows, 65536) == "rmsnorm_cluster_kernel<4>"
+        assert plain(rows, 131072) == "rmsnorm_cluster_kernel<4, plain>"
+    # 16384 < H <= 32768: up to 256 rows (RMSNorm 128), then the stash kernel.
+    assert rms_plan(0, 0, 0, 256, 32768) == "rmsnorm_cluster_kernel<4>"
+    assert rms_plan(0, 0, 0, 257, 32768) == "rmsnorm_stash_kernel<8>"
+    assert plain(128, 32768) == "rmsnorm_cluster_kernel<4, plain>"
+    assert plain(129, 32768) == "rmsnorm_stash_kernel<8, plain>"
+    # 8192 <= H <= 16384: up to 32 rows; 6144 <= H < 8192: up to 16; shorter rows never.
+    assert rms_plan(0, 0, 0, 1, 8192) == "rmsnorm_cluster_kernel<1>"  # 8 CTAs of 128 threads
+    assert rms_plan(0, 0, 0, 32, 8192) == "rmsnorm_cluster_kernel<2>"  # 4 CTAs of 128 threads
+    assert rms_plan(0, 0, 0, 33, 8192) == "rmsnorm_cta_kernel<2>"
+    assert rms_plan(0, 0, 0, 16, 6144) == "rmsnorm_cluster_kernel<1>"
+    assert rms_plan(0, 0, 0, 17, 6144) == "rmsnorm_cta_kernel<2>"
+    assert rms_plan(0, 0, 0, 1, 6136) == "rmsnorm_cta_kernel<2>"
+    assert rms_plan(0, 0, 0, 1, 4096) == "rmsnorm_cta_kernel<1>"
+    # H >= 12288, more rows than SMs up to 256 (where one CTA a row needs a second wave).
+    assert rms_plan(0, 0, 0, 148, 12288) == "rmsnorm_cta_kernel<4>"
+    assert rms_plan(0, 0, 0, 149, 12288) == "rmsnorm_cluster_kernel<2>"
+    assert rms_plan(0, 0, 0, 256, 16384) == "rmsnorm_cluster_kernel<4>"
+    assert rms_plan(0, 0, 0, 257, 16384) == "rmsnorm_stash_kernel<4>"
+    # Misaligned rows, widths not a multiple of 8 and misaligned fp8 outputs stay off it; a
+    # misaligned weight does not.
+    assert not rms_plan(1, 1, 0, 8, 65536).startswith("rmsnorm_cluster")
+    assert not rms_plan(0, 0, 0, 8, 65540).startswith("rmsnorm_cluster")
+    assert rms_plan(0, 0, 1, 8, 65536) == "rmsnorm_cluster_kernel<4>"
+    assert not capi.fused_add_rms_norm_static_fp8_quant_plan(BASE, BASE + 4096, BASE + (1 << 34) + 2, BASE + 12288,
+                                                             8, 65536).startswith("rmsnorm_cluster")
 
 
 def test_silu_plan_selection() -> None:

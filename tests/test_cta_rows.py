@@ -22,8 +22,12 @@ def _cuda() -> None:
 
 
 HIDDEN = (1032, 1536, 2048, 3584, 4096, 5120, 8192, 12288, 16384)
-CASES = [(rows, hidden, w_off) for hidden in HIDDEN for rows in (1, 3, 64, 256) for w_off in (0, 1)
-         if w_off == 0 or rows == 3]
+# Rows of 8192+ elements: row counts the planner keeps on this kernel (fewer rows, and at 12288+
+# more rows than SMs, go to the cluster kernel).
+ROWS = {hidden: (1, 3, 64, 256) if hidden < 8192 else (33, 64, 256) if hidden < 12288 else (33, 64, 148)
+        for hidden in HIDDEN}
+CASES = [(rows, hidden, w_off) for hidden in HIDDEN for rows in ROWS[hidden] for w_off in (0, 1)
+         if w_off == 0 or rows == ROWS[hidden][1]]
 # One chunk a thread: up to the rows whose CTAs an SM holds at once (148 SMs x 8 / 8 / 6 / 3 / 3).
 CASES += [(1184, 1032, 0), (1184, 1536, 1), (888, 2048, 0), (444, 3584, 0), (400, 3584, 1), (444, 4096, 0)]
 

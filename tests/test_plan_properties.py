@@ -1,7 +1,8 @@
 """Kernel selection over random shapes and pointer offsets (CPU, no device): whatever the planner
-picks, the named kernel's preconditions hold - the vector kernels only see 16-byte aligned rows
-within their width limits, the shifted kernel only the phase it is instantiated for, the staged
-kernel x and residual (or out) at the same offset and no fp8 output, and "none" means no rows."""
+picks, the named kernel's preconditions hold - the vector kernels (the cluster kernel included)
+only see 16-byte aligned rows within their width limits, the shifted kernel only the phase it is
+instantiated for, the staged kernel x and residual (or out) at the same offset and no fp8 output,
+and "none" means no rows."""
 
 from __future__ import annotations
 
@@ -16,7 +17,8 @@ BASE = 0x7F0000000000  # never dereferenced; 256-byte aligned
 
 offsets = st.integers(min_value=0, max_value=7)  # bf16 elements off a 16-byte boundary
 widths = st.one_of(st.integers(min_value=1, max_value=40000),
-                   st.sampled_from([256, 1024, 1032, 2048, 3584, 4096, 8192, 12288, 16384, 16392, 20480, 32768]))
+                   st.sampled_from([256, 1024, 1032, 2048, 3584, 4096, 6144, 8192, 12288, 16384, 16392, 20480,
+                                    32768, 32776, 65536, 131072, 131080]))
 rows_st = st.one_of(st.integers(min_value=0, max_value=300000), st.sampled_from([1, 256, 257, 444, 445, 1184, 4096]))
 
 
@@ -38,6 +40,10 @@ def check(name: str, rows: int, hidden: int, x_off: int, o_off: int, w_off: int,
         phase = int(re.match(r"rmsnorm_shifted_kernel<(\d)", name).group(1))
         assert mode != "fp8" and x_off == o_off == phase and hidden % 8 == 0 and rows > 256, name
         assert hidden <= (12288 if mode == "fused" else 4096), name
+    elif kernel == "rmsnorm_cluster_kernel":
+        assert aligned and 6144 <= hidden <= 131072, name
+        if hidden <= 32768:
+            assert rows <= 256, name  # few long rows only
     elif kernel == "rmsnorm_staged_kernel":
         assert mode != "fp8" and x_off == o_off, name
     else:

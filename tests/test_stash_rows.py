@@ -122,8 +122,9 @@ def test_graph_replay_matches_eager() -> None:
 
 # Rows of 16384 < H <= 32768: eight chunks a thread (up to 512 threads); add+RMSNorm at 96
 # registers ("capped", two CTAs an SM) up to H = 20480 for more than 256 rows, else at 128.
-LONG = [(1000, 16392, "capped"), (300, 18432, "capped"), (257, 20480, "capped"), (256, 18432, ""),
-        (100, 24576, ""), (64, 32768, "")]
+# 256 rows or fewer go to the cluster kernel.
+LONG = [(1000, 16392, "capped"), (300, 18432, "capped"), (257, 20480, "capped"), (300, 24576, ""),
+        (257, 32768, "")]
 
 
 @pytest.mark.parametrize("w_off", [0, 1])
