@@ -3,7 +3,8 @@
 The planner counts how many CTAs of the CTA-per-row kernel an SM holds at once from the registers
 its one-chunk instances are held to (40 for the bf16 ops, 64 for the fp8 op), the stash kernel's
 eight rows per SM rest on its 64-register bound, and its capped instance for rows of up to 20480
-elements on two CTAs an SM at 96 registers. A compiler that broke either, or began
+elements on two CTAs an SM at 96 registers; the cluster kernel's 2 CTAs of 512 threads an SM on its
+64-register bound. A compiler that broke any of them, or began
 to spill, would change the measured crossovers silently; this test reads the report instead.
 """
 
@@ -65,6 +66,17 @@ def test_shifted_kernel_registers() -> None:
     res = kernel_resources()
     names = [n for n in res if n.startswith("_ZN3ipl22rmsnorm_shifted_kernel")]
     assert len(names) == 14  # seven phases, add+RMSNorm and RMSNorm
+    for n in names:
+        regs, spills = res[n]
+        assert regs <= 64 and spills == 0, (n, regs, spills)
+
+
+def test_cluster_kernel_registers() -> None:
+    """Nine instances (1, 2 and 4 chunks a thread; three modes), each within the 64 registers that
+    let two CTAs of 512 threads, or four of 256, share an SM."""
+    res = kernel_resources()
+    names = [n for n in res if n.startswith("_ZN3ipl22rmsnorm_cluster_kernel")]
+    assert len(names) == 9, names
     for n in names:
         regs, spills = res[n]
         assert regs <= 64 and spills == 0, (n, regs, spills)
