@@ -1048,8 +1048,10 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_cluster_kernel(co
 // Many rows that start `kPhase` elements (1..7) into a 16-byte block, x and residual (or x and
 // out) alike; H % 8 == 0, so every row has that phase. The stash kernel's scheme on the H / 8 + 1
 // aligned 16-byte chunks that cover each row: the elements of the first and last chunk that lie
-// outside the row are masked out of the sum and not stored (those two chunks are stored element
-// by element; the neighbouring rows' CTAs only read them and discard them), and gamma is shifted
+// outside the row are masked out of the sum and not stored (those two chunks are stored in at most
+// three aligned 8-, 4- or 2-byte pieces, which the phase fixes at compile time - 1.3-4.9 % faster
+// for add+RMSNorm and 2-22 % for RMSNorm than eight checked 2-byte stores; the neighbouring rows'
+// CTAs only read them and discard them), and gamma is shifted
 // by the phase to match. The phase is a template parameter so that the shift is two aligned
 // 16-byte loads and four funnel shifts of fixed registers (with a runtime shift the kernel was
 // 2-5 % slower, with a runtime switch 5-10 %). Every loaded byte shares a 16-byte block with an
@@ -1082,6 +1084,40 @@ __device__ __forceinline__ U32x4 shifted_gamma_chunk(const uint16_t* weight, int
         g.v[i] = lo | (hi << 16);
     }
     return g;
+}
+
+// Elements [kLo, kHi) of a 16-byte aligned chunk, stored with the widest aligned stores that fit
+// (8, 4 or 2 bytes): at most three stores for any span of a chunk.
+template <int kLo, int kHi>
+__device__ __forceinline__ void store_span(uint16_t* chunk, const U32x4& w) {
+    if constexpr (kLo < kHi) {
+        if constexpr (kLo % 4 == 0 && kLo + 4 <= kHi) {
+            st_v2(chunk + kLo, w.v[kLo / 2], w.v[kLo / 2 + 1]);
+            store_span<kLo + 4, kHi>(chunk, w);
+        } else if constexpr (kLo % 2 == 0 && kLo + 2 <= kHi) {
+            asm volatile("st.global.b32 [%0], %1;" ::"l"(chunk + kLo), "r"(w.v[kLo / 2]) : "memory");
+            store_span<kLo + 2, kHi>(chunk, w);
+        } else {
+            const uint16_t e = static_cast<uint16_t>((kLo & 1) ? (w.v[kLo / 2] >> 16) : (w.v[kLo / 2] & 0xffffu));
+            asm volatile("st.global.b16 [%0], %1;" ::"l"(chunk + kLo), "h"(e) : "memory");
+            store_span<kLo + 1, kHi>(chunk, w);
+        }
+    }
+}
+
+// Zeroes elements [kLo, kHi) of a chunk's values (those outside the row).
+template <int kLo, int kHi>
+__device__ __forceinline__ void zero_span(Pairs4& v) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const bool lo_out = 2 * i >= kLo && 2 * i < kHi;
+        const bool hi_out = 2 * i + 1 >= kLo && 2 * i + 1 < kHi;
+        if (lo_out || hi_out) {
+            float lo, hi;
+            f32x2_split(v.v[i], lo, hi);
+            v.v[i] = f32x2_make(lo_out ? 0.0f : lo, hi_out ? 0.0f : hi);
+        }
+    }
 }
 
 template <int kMode, int kPhase>
@@ -1129,10 +1165,23 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_shifted_kernel(co
         for (int u = 0; u < kUnroll; ++u) {
             const int c = threadIdx.x + u * threads;
             if (c < chunks) {
+                // The first chunk (thread 0's first) holds elements [kPhase, 8) of the row, the
+                // last elements [0, kPhase); both are stored piecewise.
                 Pairs4 v = kResidual ? chunk_sum(xs[u], rs[u]) : chunk_widen(xs[u]);
-                const bool full = c != 0 && c != chunks - 1;
-                if (!full) mask_outside(v, 8 * c - kPhase, p.hidden);
-                if constexpr (kResidual) store_chunk(rr + 8 * c, chunk_to_bf16(v), full, 8 * c - kPhase, p.hidden);
+                const bool head = u == 0 && threadIdx.x == 0;
+                const bool tail = c == chunks - 1;
+                if (head) zero_span<0, kPhase>(v);
+                if (tail) zero_span<kPhase, 8>(v);
+                if constexpr (kResidual) {
+                    const U32x4 out = chunk_to_bf16(v);
+                    if (head) {
+                        store_span<kPhase, 8>(rr + 8 * c, out);
+                    } else if (tail) {
+                        store_span<0, kPhase>(rr + 8 * c, out);
+                    } else {
+                        st_v4(rr + 8 * c, out);
+                    }
+                }
 #pragma unroll
                 for (int e = 0; e < 4; ++e) acc = f32x2_fma(v.v[e], v.v[e], acc);
             }
@@ -1155,7 +1204,14 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_shifted_kernel(co
                 const Pairs4 w = chunk_widen(shifted_gamma_chunk<kPhase>(p.weight, c, p.hidden, weight_aligned));
 #pragma unroll
                 for (int e = 0; e < 4; ++e) v.v[e] = f32x2_mul(f32x2_mul(v.v[e], inv2), w.v[e]);
-                store_chunk(orow + 8 * c, chunk_to_bf16(v), c != 0 && c != chunks - 1, 8 * c - kPhase, p.hidden);
+                const U32x4 out = chunk_to_bf16(v);
+                if (u == 0 && threadIdx.x == 0) {
+                    store_span<kPhase, 8>(orow + 8 * c, out);
+                } else if (c == chunks - 1) {
+                    store_span<0, kPhase>(orow + 8 * c, out);
+                } else {
+                    st_v4(orow + 8 * c, out);
+                }
             }
         }
     }
