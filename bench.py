@@ -22,7 +22,8 @@ A step is one call of the op on one batch already resident in HBM:
 
 Unless ``--no-subrecords``, the line for the default workload also carries ``sharded``,
 ``misaligned`` and ``silu`` records: the other three workloads measured the same way in the same
-run, each with its kernel, timings, roofline fraction and an oracle check of its outputs.
+run, each with its kernel, timings, roofline fraction and an oracle check of its outputs, and on
+one GPU the reference's CPU path timed on the same workload (1024 rows of the sharded one).
 
 Timing: W warm-up steps; then, while the device is held by a short sleep kernel (NVBench's
 blocking-kernel method), the host enqueues W more warm-up steps, the start event, the K timed
@@ -822,6 +823,12 @@ def run_ours(args, spec) -> None:
                                       "source": traffic["command"]}
                 else:
                     rec["traffic"] = None
+                # The reference's CPU path beside each record (one GPU only, like the line's own):
+                # the full batch, or 1024 rows of the row-sharded workload; a quarter of the time.
+                if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+                    rec["cpu_baseline"] = cpu_reference_rate(
+                        sub_spec, max(0.5, args.cpu_seconds / 4),
+                        sample_rows=1024 if sub_spec.get("sharded") else sub_spec["rows"])
                 subrecords[key] = public(rec)
                 del rec
                 torch.cuda.empty_cache()

@@ -91,7 +91,10 @@ def test_our_arm_prints_the_full_contract_line_on_a_gpu() -> None:
         assert sub["kernel"].startswith(kernel_prefix), (key, sub["kernel"])
         assert sub["parity"]["parity_ok"] and sub["parity"]["parity_ok_all_ranks"], (key, sub["parity"])
         assert sub["value"] > 0 and 0.1 < sub["roofline_frac"] < 1.3 and sub["launch"]["queued_before_start"]
+        cpu = sub["cpu_baseline"]  # the reference's CPU path beside each record
+        assert cpu["value"] > 0 and cpu["cores"] >= 1 and cpu["kind"] == "port" and cpu["rows_per_s"] > 0
     assert d["sharded"]["rows_per_rank"] == 262144 and d["sharded"]["parity"]["rows_checked"] >= 64
+    assert d["sharded"]["cpu_baseline"]["sample"].startswith("1024 rows")
 
 
 @pytest.mark.gpu
