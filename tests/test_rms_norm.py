@@ -145,3 +145,42 @@ def test_vllm_providers_dispatch_to_the_b200_kernels() -> None:
         y = plain(x, w, eps, None)
     assert_close_to_oracle(y, oracle.c_rms_norm(oracle.tensor_bits(x), oracle.tensor_bits(w), eps), "vLLM rms_norm")
     torch.testing.assert_close(y, plain.impls["native"].impl_fn(x, w, eps, None), rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("tokens, hidden", [(8, 8192), (16, 16384), (4, 65536)])
+@torch.inference_mode()
+def test_vllm_provider_runs_the_cluster_kernel_on_long_decode_rows(tokens: int, hidden: int) -> None:
+    """Decode batches of long rows through vLLM's IR ops reach the cluster kernel (each row split
+    over a thread-block cluster) and match the oracle."""
+    pytest.importorskip("vllm.ir")
+    from vllm import ir
+
+    from inference_performance_lab.kernels import vllm_plugin
+
+    vllm_plugin.register()
+    generator = torch.Generator(device="cuda").manual_seed(tokens + hidden)
+    x = torch.randn(tokens, hidden, device="cuda", generator=generator).to(torch.bfloat16)
+    r = torch.randn(tokens, hidden, device="cuda", generator=generator).to(torch.bfloat16)
+    w = (torch.randn(hidden, device="cuda", generator=generator) * 0.1 + 1).to(torch.bfloat16)
+    eps = 1e-6
+    assert capi.fused_add_rms_norm_plan(x.data_ptr(), r.data_ptr(), w.data_ptr(), tokens, hidden).startswith(
+        "rmsnorm_cluster_kernel")
+    fused = ir.ops.fused_add_rms_norm
+    with fused.set_priority([vllm_plugin.PROVIDER, "native"]):
+        assert fused.dispatch(x, r, w, eps, None).provider == vllm_plugin.PROVIDER
+        out, res = fused.maybe_inplace(x.clone(), r.clone(), w, eps, None)
+    expected_out, expected_res = oracle.c_fused_add_rms_norm(
+        oracle.tensor_bits(x), oracle.tensor_bits(r), oracle.tensor_bits(w), eps
+    )
+    np.testing.assert_array_equal(oracle.tensor_bits(res), expected_res)
+    assert_close_to_oracle(out, expected_out, f"vLLM fused_add_rms_norm {tokens}x{hidden}")
+
+    plain = ir.ops.rms_norm
+    out_plan = torch.empty_like(x)
+    assert capi.rms_norm_plan(out_plan.data_ptr(), x.data_ptr(), w.data_ptr(), tokens, hidden).startswith(
+        "rmsnorm_cluster_kernel")
+    with plain.set_priority([vllm_plugin.PROVIDER, "native"]):
+        assert plain.dispatch(x, w, eps, None).provider == vllm_plugin.PROVIDER
+        y = plain(x, w, eps, None)
+    assert_close_to_oracle(y, oracle.c_rms_norm(oracle.tensor_bits(x), oracle.tensor_bits(w), eps),
+                           f"vLLM rms_norm {tokens}x{hidden}")
