@@ -166,3 +166,24 @@ def test_every_cta_of_a_row_normalises_with_the_same_scale() -> None:
     assert_close_to_oracle(ax, out, "output")
     gx.assert_guards_intact()
     gr.assert_guards_intact()
+
+
+@pytest.mark.parametrize("scale", [300.0, 1e-4])
+@pytest.mark.parametrize("rows, hidden", [(2, 65536), (8, 16384)])
+@torch.inference_mode()
+def test_extreme_magnitudes(rows: int, hidden: int, scale: float) -> None:
+    """The golden vectors' large- and small-magnitude recipes (x and residual scaled by 300 and by
+    1e-4, where eps dominates the mean of squares) at widths the cluster kernel takes."""
+    x, r, w = _inputs(rows, hidden, int(scale * 7) + hidden)
+    x = (x.float() * scale).to(torch.bfloat16)
+    r = (r.float() * scale).to(torch.bfloat16)
+    gx, gr = Guarded(x.shape, 0), Guarded(x.shape, 0)
+    ax, ar = gx.load(oracle.tensor_bits(x)), gr.load(oracle.tensor_bits(r))
+    assert capi.fused_add_rms_norm_plan(ax.data_ptr(), ar.data_ptr(), w.data_ptr(), rows, hidden).startswith(
+        "rmsnorm_cluster_kernel")
+    torch.ops.inference_performance_lab.fused_add_rms_norm(ax, ar, w, 1e-6)
+    out, res = oracle.c_fused_add_rms_norm(oracle.tensor_bits(x), oracle.tensor_bits(r), oracle.tensor_bits(w), 1e-6)
+    assert_bits_equal(ar, res, f"{rows}x{hidden} x{scale:g} residual")
+    assert_close_to_oracle(ax, out, f"{rows}x{hidden} x{scale:g} output")
+    gx.assert_guards_intact()
+    gr.assert_guards_intact()
