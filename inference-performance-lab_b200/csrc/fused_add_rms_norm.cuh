@@ -918,6 +918,120 @@ __global__ void __launch_bounds__(kCapped ? kStashCappedThreads : kStashMaxThrea
 }
 
 // ---------------------------------------------------------------------------------------------
+// The stash kernel's scheme with 256-bit accesses, for add+RMSNorm and its fp8 output: a CTA for
+// every row of H / 16 threads (rounded up to a warp), each owning one pair of adjacent 16-byte
+// chunks - a 32-byte load of x and of residual, 32-byte stores of residual and x (16 bytes of e4m3
+// for the fp8 op) - and staging its 32 bytes of gamma in shared memory by cp.async (the planner
+// gives it a 16-byte aligned weight only: a fallback for another weight cost the kernel 3-4 %
+// through its registers and schedule). Half the load and store instructions of four 16-byte
+// chunks a thread, and smaller CTAs (half the bytes in flight each), so a CTA retires sooner. For
+// 1536 <= H <= 5120, H % 16 == 0, 32-byte aligned rows and 257-4096 rows, measured on B200 (cold
+// L2, CUDA graph, every CTA looking one wave ahead) against the four-chunk instance: 1.02-1.21x
+// (2048 x 3584 8.96 against 9.34 us, 2048 x 2048 5.39 against 6.51), and 1.02-1.12x against the
+// CTA-per-row kernel on the one-wave launches it had taken. At H = 6144 and beyond, or past 4096
+// rows with only the first wave looking ahead, it fell behind; plain RMSNorm did too.
+constexpr int kStashV8MinHidden = 1536;
+constexpr int kStashV8MaxHidden = 5120;  // 320 threads
+constexpr int64_t kStashV8MaxRows = 4096;
+
+template <int kMode>
+__global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_stash_v8_kernel(const WarpRowParams p) {
+    constexpr bool kResidual = kMode != kModePlain;
+    constexpr bool kFp8 = kMode == kModeFusedFp8;
+    __shared__ float partials[2][kStashMaxThreads / kWarpSize];
+    extern __shared__ __align__(16) unsigned char gamma_smem[];  // H * 2 bytes: gamma, as in the weight
+    const int warps = static_cast<int>(blockDim.x) / kWarpSize;
+    const int q = threadIdx.x;  // this thread's pair: chunks 2q and 2q + 1
+    const bool active = q < (p.hidden >> 4);
+    const int warp = threadIdx.x / kWarpSize;
+    const int lane = threadIdx.x % kWarpSize;
+    const float hidden_f = static_cast<float>(p.hidden);
+    const uint32_t gamma_base = smem_addr(gamma_smem) + 32u * static_cast<uint32_t>(q);
+
+    prefetch_first_row<kResidual>(p);
+    grid_dependency_wait();
+    grid_launch_dependents();
+    prefetch_next_wave_row<kResidual>(p);
+    if (active) {
+        cp_async_16(gamma_base, p.weight + 16 * q);
+        cp_async_16(gamma_base + 16u, p.weight + 16 * q + 8);
+    }
+    const float scale_inv = kFp8 ? 1.0f / *p.scale : 1.0f;
+    const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
+
+    int parity = 0;
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const uint16_t* xr = p.x + row * p.hidden + 16 * q;
+        uint16_t* rr = kResidual ? p.residual + row * p.hidden + 16 * q : nullptr;
+        U32x8 xs, rs;
+        F32x2 acc = f32x2_make(0.0f, 0.0f);
+        if (active) {
+            xs = ld_v8(xr);
+            if constexpr (kResidual) rs = ld_v8(rr);
+            const U32x4 x0 = {{xs.v[0], xs.v[1], xs.v[2], xs.v[3]}}, x1 = {{xs.v[4], xs.v[5], xs.v[6], xs.v[7]}};
+            Pairs4 a, b;
+            if constexpr (kResidual) {
+                a = chunk_sum(x0, {{rs.v[0], rs.v[1], rs.v[2], rs.v[3]}});
+                b = chunk_sum(x1, {{rs.v[4], rs.v[5], rs.v[6], rs.v[7]}});
+                const U32x4 ra = chunk_to_bf16(a), rb = chunk_to_bf16(b);
+                st_v8(rr, {{ra.v[0], ra.v[1], ra.v[2], ra.v[3], rb.v[0], rb.v[1], rb.v[2], rb.v[3]}});
+            } else {
+                a = chunk_widen(x0);
+                b = chunk_widen(x1);
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc = f32x2_fma(a.v[e], a.v[e], acc);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc = f32x2_fma(b.v[e], b.v[e], acc);
+        }
+        float acc_lo, acc_hi;
+        f32x2_split(acc, acc_lo, acc_hi);
+        const float warp_total = warp_sum(acc_lo + acc_hi);
+        if (lane == 0) partials[parity][warp] = warp_total;  // two parities: see rmsnorm_cta_kernel
+        cp_async_wait_all();
+        __syncthreads();
+        float sumsq = 0.0f;
+        for (int w = 0; w < warps; ++w) sumsq += partials[parity][w];
+        parity ^= 1;
+        const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
+        const F32x2 inv2 = f32x2_make(inv, inv);
+        if (active) {
+            const U32x4 x0 = {{xs.v[0], xs.v[1], xs.v[2], xs.v[3]}}, x1 = {{xs.v[4], xs.v[5], xs.v[6], xs.v[7]}};
+            Pairs4 a, b;
+            if constexpr (kResidual) {
+                a = chunk_sum(x0, {{rs.v[0], rs.v[1], rs.v[2], rs.v[3]}});
+                b = chunk_sum(x1, {{rs.v[4], rs.v[5], rs.v[6], rs.v[7]}});
+            } else {
+                a = chunk_widen(x0);
+                b = chunk_widen(x1);
+            }
+            const Pairs4 wa = chunk_widen(lds_v4(gamma_base));
+            const Pairs4 wb = chunk_widen(lds_v4(gamma_base + 16u));
+#pragma unroll
+            for (int e = 0; e < 4; ++e) a.v[e] = f32x2_mul(f32x2_mul(a.v[e], inv2), wa.v[e]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) b.v[e] = f32x2_mul(f32x2_mul(b.v[e], inv2), wb.v[e]);
+            if constexpr (kFp8) {
+                // 16 e4m3 bytes; the planner gives this kernel a 16-byte aligned fp8 output.
+#pragma unroll
+                for (int e = 0; e < 4; ++e) a.v[e] = f32x2_mul(a.v[e], scale_inv2);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) b.v[e] = f32x2_mul(b.v[e], scale_inv2);
+                const U32x4 o = {{f32x2_to_e4m3x2(a.v[0]) | (f32x2_to_e4m3x2(a.v[1]) << 16),
+                                  f32x2_to_e4m3x2(a.v[2]) | (f32x2_to_e4m3x2(a.v[3]) << 16),
+                                  f32x2_to_e4m3x2(b.v[0]) | (f32x2_to_e4m3x2(b.v[1]) << 16),
+                                  f32x2_to_e4m3x2(b.v[2]) | (f32x2_to_e4m3x2(b.v[3]) << 16)}};
+                st_v4(p.out8 + row * p.hidden + 16 * q, o);
+            } else {
+                const U32x4 oa = chunk_to_bf16(a), ob = chunk_to_bf16(b);
+                st_v8(p.out + row * p.hidden + 16 * q,
+                      {{oa.v[0], oa.v[1], oa.v[2], oa.v[3], ob.v[0], ob.v[1], ob.v[2], ob.v[3]}});
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 // A row split over a thread-block cluster (H % 8 == 0, 16-byte aligned rows): the C CTAs of a
 // cluster (2..8, along x; grid = rows * C) share one row, CTA k owning its 16-byte chunks
 // [k * S, min((k + 1) * S, H / 8)), S = p.cluster_slice, in registers as in the stash kernel

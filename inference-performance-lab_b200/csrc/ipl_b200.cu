@@ -122,7 +122,7 @@ cudaError_t launch_clustered(Kernel kernel, unsigned grid, unsigned cluster, uns
 // ------------------------------------------------------------------------------------------
 // add + RMSNorm / RMSNorm planning
 
-enum class RmsFamily { kNone, kStaged, kWarpRow, kCtaRow, kStash, kShifted, kCluster, kRowwiseCached, kRowwiseTwoPass };
+enum class RmsFamily { kNone, kStaged, kWarpRow, kCtaRow, kStash, kStashV8, kShifted, kCluster, kRowwiseCached, kRowwiseTwoPass };
 
 struct RmsPlan {
     RmsFamily family = RmsFamily::kNone;
@@ -198,6 +198,10 @@ const char* rms_kernel_name(const RmsPlan& plan, int mode) {
         case RmsFamily::kCluster:
             while ((1 << i) < plan.chunks_per_lane) ++i;
             return kClusterNames[mode][i];
+        case RmsFamily::kStashV8: {
+            return mode == kModeFused ? "rmsnorm_stash_v8_kernel" : mode == kModeFusedFp8 ? "rmsnorm_stash_v8_kernel<fp8>"
+                                                                                        : "invalid";
+        }
         case RmsFamily::kRowwiseCached: return kRowwiseNames[mode][0];
         case RmsFamily::kRowwiseTwoPass: return kRowwiseNames[mode][1];
     }
@@ -300,9 +304,10 @@ int cluster_ctas_for(int64_t rows, int64_t hidden, int mode, int sm_count) {
 // Pure function of the arguments and two device limits. `other` is the residual (fused modes) or
 // the output (plain mode); either must share x's offset modulo 16 bytes for the staged kernel.
 // `out8` is the fp8 output of kModeFusedFp8, whose vector paths need 16-byte aligned rows
-// (H % 8 == 0) and an 8-byte aligned output.
-RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t rows, int64_t hidden, int mode,
-                 int sm_count, int smem_limit) {
+// (H % 8 == 0) and an 8-byte aligned output. `weight` matters only to the 256-bit stash kernel,
+// which stages it with 16-byte copies.
+RmsPlan plan_rms(const void* x, const void* other, const void* out8, const void* weight, int64_t rows,
+                 int64_t hidden, int mode, int sm_count, int smem_limit) {
     RmsPlan plan;
     if (rows == 0) return plan;
     const bool residual = mode != kModePlain;
@@ -325,6 +330,29 @@ RmsPlan plan_rms(const void* x, const void* other, const void* out8, int64_t row
             set_cluster(plan, rows, hidden, ctas);
             return plan;
         }
+    }
+    // Add+RMSNorm (and its fp8 output) on rows of 1536 <= H <= 5120 (H % 16 == 0, x and residual
+    // 32-byte aligned, weight and an fp8 output 16-byte aligned), 257-4096 of them: the stash
+    // scheme with one 32-byte pair of chunks a thread (rmsnorm_stash_v8_kernel), every CTA looking
+    // one resident wave ahead. Measured against the kernels below on B200 (cold L2, CUDA graph):
+    // add+RMSNorm 1.02-1.21x the four-chunk stash instance (2048 x 3584 8.96 against 9.34 us,
+    // 2000 x 3072 7.44 against 8.29) and the CTA-per-row kernel on its one-wave launches (300 x 3584
+    // 2.72 against 3.06); the fp8 output 1.01-1.08x. Plain RMSNorm stays on the four-chunk stash
+    // instance (0.96x at 2048 x 3584).
+    if (mode != kModePlain && hidden % 16 == 0 && hidden >= kStashV8MinHidden && hidden <= kStashV8MaxHidden &&
+        rows > kCtaRowMaxRows && rows <= kStashV8MaxRows && ((xa | oa) & 31u) == 0 &&
+        (reinterpret_cast<uintptr_t>(weight) & 15u) == 0 &&
+        (mode != kModeFusedFp8 || (reinterpret_cast<uintptr_t>(out8) & 15u) == 0)) {
+        const int64_t threads = (hidden / 16 + kWarpSize - 1) / kWarpSize * kWarpSize;
+        plan.family = RmsFamily::kStashV8;
+        plan.chunks_per_lane = 2;
+        plan.threads = static_cast<unsigned>(threads);
+        plan.smem = static_cast<size_t>(hidden) * 2u;
+        plan.grid = static_cast<unsigned>(rows);
+        const int64_t wave = resident_ctas(sm_count, threads, 64);  // launch bound (512, 2): 64 registers
+        plan.lookahead = rows > wave ? wave : 0;
+        plan.lookahead_ctas = rows > wave ? rows : 0;  // every CTA: up to 4096 rows is a few waves
+        return plan;
     }
     // Aligned rows (H % 8 == 0, 16-byte aligned, H <= 16384) have four kernels. The choice, from
     // cold-L2 sweeps on B200 against each other and vLLM's kernels (1..262144 rows, H 128..16384):
@@ -551,7 +579,7 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8
     ipl_status st = current_device(&device, &info);
     if (st != IPL_SUCCESS) return st;
     RmsPlan plan = plan_rms(x, kResidual ? static_cast<const void*>(residual) : static_cast<const void*>(out), out8,
-                            rows, hidden, kMode, info->sm_count.load(std::memory_order_relaxed),
+                            weight, rows, hidden, kMode, info->sm_count.load(std::memory_order_relaxed),
                             info->max_smem_optin.load(std::memory_order_relaxed));
     plan.staged.x = x;
     plan.staged.residual = residual;
@@ -620,6 +648,19 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8
                     case 6: err = launch(rmsnorm_shifted_kernel<kMode, 6>, plan.grid, plan.threads, 0, stream, w); break;
                     default: err = launch(rmsnorm_shifted_kernel<kMode, 7>, plan.grid, plan.threads, 0, stream, w); break;
                 }
+                if (err != cudaSuccess) {
+                    return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
+                }
+                return IPL_SUCCESS;
+            }
+        }
+        case RmsFamily::kStashV8: {
+            if constexpr (kMode == kModePlain) {
+                return fail(IPL_ERROR_CUDA, "%s: no 256-bit stash plan exists for this mode", mode_label(kMode));
+            } else {
+                const WarpRowParams w = row_params(plan);
+                const cudaError_t err =
+                    launch(rmsnorm_stash_v8_kernel<kMode>, plan.grid, plan.threads, plan.smem, stream, w);
                 if (err != cudaSuccess) {
                     return fail(IPL_ERROR_CUDA, "%s kernel launch failed: %s", mode_label(kMode), cudaGetErrorString(err));
                 }
@@ -873,7 +914,7 @@ const char* ipl_fused_add_rms_norm_plan(const void* x, const void* residual, con
     if (check_rms_args(x, residual, weight, rows, hidden_size, 1.0, true) != IPL_SUCCESS) return "invalid";
     int sms = 0, smem = 0;
     plan_limits(&sms, &smem);
-    return rms_kernel_name(plan_rms(x, residual, nullptr, rows, hidden_size, kModeFused, sms, smem), kModeFused);
+    return rms_kernel_name(plan_rms(x, residual, nullptr, weight, rows, hidden_size, kModeFused, sms, smem), kModeFused);
 }
 
 const char* ipl_rms_norm_plan(const void* output, const void* input, const void* weight, int64_t rows,
@@ -881,7 +922,7 @@ const char* ipl_rms_norm_plan(const void* output, const void* input, const void*
     if (check_rms_args(input, output, weight, rows, hidden_size, 1.0, false) != IPL_SUCCESS) return "invalid";
     int sms = 0, smem = 0;
     plan_limits(&sms, &smem);
-    return rms_kernel_name(plan_rms(input, output, nullptr, rows, hidden_size, kModePlain, sms, smem), kModePlain);
+    return rms_kernel_name(plan_rms(input, output, nullptr, weight, rows, hidden_size, kModePlain, sms, smem), kModePlain);
 }
 
 const char* ipl_fused_add_rms_norm_static_fp8_quant_plan(const void* output, const void* input, const void* residual,
@@ -891,7 +932,7 @@ const char* ipl_fused_add_rms_norm_static_fp8_quant_plan(const void* output, con
     }
     int sms = 0, smem = 0;
     plan_limits(&sms, &smem);
-    return rms_kernel_name(plan_rms(input, residual, output, rows, hidden_size, kModeFusedFp8, sms, smem),
+    return rms_kernel_name(plan_rms(input, residual, output, weight, rows, hidden_size, kModeFusedFp8, sms, smem),
                            kModeFusedFp8);
 }
 

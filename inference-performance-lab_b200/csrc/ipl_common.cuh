@@ -141,6 +141,15 @@ __device__ __forceinline__ U32x4 ld_v4(const void* p) {
                  : "l"(p));
     return r;
 }
+// Coherent 32-byte load (256-bit, sm_100), not allocating in L1; p 32-byte aligned.
+__device__ __forceinline__ U32x8 ld_v8(const void* p) {
+    U32x8 r;
+    asm volatile("ld.global.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3]), "=r"(r.v[4]), "=r"(r.v[5]),
+                   "=r"(r.v[6]), "=r"(r.v[7])
+                 : "l"(p));
+    return r;
+}
 // Read-only 16-byte load that may stay in L1 (data every CTA on the SM reads, e.g. gamma).
 __device__ __forceinline__ U32x4 ld_shared_ro_v4(const void* p) {
     U32x4 r;

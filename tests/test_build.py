@@ -71,6 +71,16 @@ def test_shifted_kernel_registers() -> None:
         assert regs <= 64 and spills == 0, (n, regs, spills)
 
 
+def test_stash_v8_kernel_registers() -> None:
+    """The 256-bit stash kernel's two instances (add+RMSNorm, fp8 output) within 64 registers."""
+    res = kernel_resources()
+    names = [n for n in res if n.startswith("_ZN3ipl23rmsnorm_stash_v8_kernel")]
+    assert len(names) == 2, names
+    for n in names:
+        regs, spills = res[n]
+        assert regs <= 64 and spills == 0, (n, regs, spills)
+
+
 def test_cluster_kernel_registers() -> None:
     """Nine instances (1, 2 and 4 chunks a thread; three modes), each within the 64 registers that
     let two CTAs of 512 threads, or four of 256, share an SM."""

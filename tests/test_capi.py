@@ -80,7 +80,7 @@ def test_c_caller_builds_links_and_runs(tmp_path: Path) -> None:
                     "-L", str(lib.parent), "-l:" + lib.name, "-Wl,-rpath," + str(lib.parent), "-o", str(exe)],
                    check=True, capture_output=True, text=True)
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines()
-    assert out[0] == "rmsnorm_stash_kernel<4>"
+    assert out[0] == "rmsnorm_stash_v8_kernel"
     assert out[1] == "silu_vector_kernel<32>"
     assert out[2] == "IPL_ERROR_INVALID_VALUE: epsilon must be positive"
     assert out[3].startswith("IPL_ERROR_MISALIGNED: ") and "divisible by 8" in out[3]
@@ -155,7 +155,9 @@ def test_fp8_quant_arguments_and_plans() -> None:
     with pytest.raises(capi.IplError, match="epsilon must be positive"):
         capi.fused_add_rms_norm_static_fp8_quant(BASE, BASE + 4096, BASE + 8192, BASE + 12288, BASE, 4, 16, 0.0)
     plan = capi.fused_add_rms_norm_static_fp8_quant_plan
-    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 3584) == "rmsnorm_stash_kernel<4, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 3584) == "rmsnorm_stash_v8_kernel<fp8>"
+    assert plan(BASE + 8, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 3584) == "rmsnorm_stash_kernel<4, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12290, 2048, 3584) == "rmsnorm_stash_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 262144, 8192) == "rmsnorm_stash_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 16384) == "rmsnorm_stash_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 600, 18432) == "rmsnorm_stash_kernel<8, fp8, capped>"
@@ -170,9 +172,11 @@ def test_fp8_quant_arguments_and_plans() -> None:
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 2048, 1024) == "rmsnorm_stash_kernel<4, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 7, 3584) == "rmsnorm_cta_kernel<1, fp8>"
     assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 9000, 4096) == "rmsnorm_stash_kernel<4, fp8>"
-    # The fp8 op's one-chunk CTA holds 64 registers: 2 CTAs of 448 threads an SM at H = 3584.
-    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 296, 3584) == "rmsnorm_cta_kernel<1, fp8>"
-    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 297, 3584) == "rmsnorm_stash_kernel<4, fp8>"
+    # The fp8 op's one-chunk CTA holds 64 registers: 2 CTAs of 448 threads an SM at H = 3584 (where
+    # the 256-bit stash kernel does not apply: here a weight off 16 bytes).
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12290, 296, 3584) == "rmsnorm_cta_kernel<1, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12290, 297, 3584) == "rmsnorm_stash_kernel<4, fp8>"
+    assert plan(BASE, BASE + 4096, BASE + (1 << 34), BASE + 12288, 296, 3584) == "rmsnorm_stash_v8_kernel<fp8>"
     # fp8 vector stores need 16-byte aligned rows and an 8-byte aligned output.
     assert plan(BASE + 4, BASE + 4098, BASE + (1 << 34) + 2, BASE + 12288, 2048, 3584).startswith(
         "rmsnorm_rowwise_kernel"
@@ -221,8 +225,10 @@ def rms_plan(x_off: int, r_off: int, w_off: int, rows: int, hidden: int) -> str:
 
 
 def test_rms_plan_selection() -> None:
-    # 2048 x 3584 aligned (the bench workload): a 128-thread CTA per row, four chunks a thread.
-    assert rms_plan(0, 0, 0, 2048, 3584) == "rmsnorm_stash_kernel<4>"
+    # 2048 x 3584 aligned (the bench workload): a 224-thread CTA per row, one 32-byte pair of chunks
+    # a thread; with a weight off 16 bytes, 128 threads of four 16-byte chunks.
+    assert rms_plan(0, 0, 0, 2048, 3584) == "rmsnorm_stash_v8_kernel"
+    assert rms_plan(0, 0, 1, 2048, 3584) == "rmsnorm_stash_kernel<4>"
     # x and residual both off 16 bytes alike, more than 256 rows: the shifted kernel, one instance
     # per phase, up to H = 12288; fewer rows or longer ones: the staged kernel.
     for off in range(1, 8):
@@ -245,22 +251,36 @@ def test_rms_plan_selection() -> None:
     assert rms_plan(0, 0, 0, 5, 2048) == "rmsnorm_cta_kernel<1>"
     assert rms_plan(0, 0, 0, 64, 2056) == "rmsnorm_cta_kernel<1>"
     # One chunk a thread (H <= 4096): the CTA per row also while every row's CTA is resident at once
-    # - 148 SMs x 3 CTAs of 448 threads at H = 3584, x 6 of 256 at 2048, x 8 of 192 at 1536.
+    # - 148 SMs x 3 CTAs of 448 threads at H = 3584, x 6 of 256 at 2048, x 8 of 192 at 1536 - where
+    # the 256-bit stash kernel does not apply (here: a weight off 16 bytes; below H = 1536).
     for rows in (257, 148 * 2, 148 * 3):
-        assert rms_plan(0, 0, 0, rows, 3584) == "rmsnorm_cta_kernel<1>"
-    assert rms_plan(0, 0, 0, 148 * 3, 4096) == "rmsnorm_cta_kernel<1>"
-    assert rms_plan(0, 0, 0, 148 * 6, 2048) == "rmsnorm_cta_kernel<1>"
-    assert rms_plan(0, 0, 0, 148 * 8, 1536) == "rmsnorm_cta_kernel<1>"
+        assert rms_plan(0, 0, 1, rows, 3584) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 1, 148 * 3, 4096) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 1, 148 * 6, 2048) == "rmsnorm_cta_kernel<1>"
+    assert rms_plan(0, 0, 1, 148 * 8, 1536) == "rmsnorm_cta_kernel<1>"
     assert rms_plan(0, 0, 0, 148 * 8, 1032) == "rmsnorm_cta_kernel<1>"  # at most 8 CTAs an SM counted
     assert rms_plan(0, 0, 0, 148 * 8 + 1, 1032) == "rmsnorm_stash_kernel<4>"
-    assert rms_plan(0, 0, 0, 257, 5120) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 1, 257, 5120) == "rmsnorm_stash_kernel<4>"
+    # 257-4096 aligned rows of 1536-5120 elements (H % 16 == 0, 16-byte aligned weight): the
+    # 256-bit stash kernel, the cta kernel's one-wave launches included.
+    for rows in (257, 148 * 3, 148 * 3 + 1, 2048, 4096):
+        for hidden in (1536, 2048, 2560, 3584, 4096, 5120):
+            assert rms_plan(0, 0, 0, rows, hidden) == "rmsnorm_stash_v8_kernel"
+    assert rms_plan(0, 0, 0, 2048, 5136) == "rmsnorm_stash_kernel<4>"  # wider
+    assert rms_plan(0, 0, 0, 2048, 1528) == "rmsnorm_stash_kernel<4>"  # narrower
+    assert rms_plan(0, 0, 0, 2048, 3592) == "rmsnorm_stash_kernel<4>"  # H % 16 != 0
+    assert capi.fused_add_rms_norm_plan(BASE + 16, BASE + (1 << 34) + 16, BASE + (1 << 35), 2048, 3584) == \
+        "rmsnorm_stash_kernel<4>"  # rows 16 bytes off 32
+    assert capi.rms_norm_plan(BASE, BASE + (1 << 34), BASE + 8192, 2048, 3584) == "rmsnorm_stash_kernel<4, plain>"
     # More rows, up to 12288 elements each: a small CTA for every row (128 threads of four chunks
     # at H = 3584), the row-sharded workload's 2^28-element shards included.
-    for rows in (148 * 3 + 1, 148 * 6, 148 * 7, 148 * 14, 148 * 14 + 1, 148 * 16, 32768):
+    for rows in (4097, 148 * 28, 32768):
         assert rms_plan(0, 0, 0, rows, 3584) == "rmsnorm_stash_kernel<4>"
-    assert rms_plan(0, 0, 0, 148 * 14, 4096) == "rmsnorm_stash_kernel<4>"
-    assert rms_plan(0, 0, 0, 148 * 6 + 1, 2048) == "rmsnorm_stash_kernel<4>"
-    assert rms_plan(0, 0, 0, 148 * 8 + 1, 1536) == "rmsnorm_stash_kernel<4>"
+    for rows in (148 * 3 + 1, 148 * 6, 148 * 14, 148 * 16):
+        assert rms_plan(0, 0, 1, rows, 3584) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 0, 148 * 28, 4096) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 1, 148 * 6 + 1, 2048) == "rmsnorm_stash_kernel<4>"
+    assert rms_plan(0, 0, 1, 148 * 8 + 1, 1536) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 16384, 8192) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 20000, 12288) == "rmsnorm_stash_kernel<4>"
     assert rms_plan(0, 0, 0, 262144, 8192) == "rmsnorm_stash_kernel<4>"

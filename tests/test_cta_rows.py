@@ -28,8 +28,9 @@ ROWS = {hidden: (1, 3, 64, 256) if hidden < 8192 else (33, 64, 256) if hidden < 
         for hidden in HIDDEN}
 CASES = [(rows, hidden, w_off) for hidden in HIDDEN for rows in ROWS[hidden] for w_off in (0, 1)
          if w_off == 0 or rows == ROWS[hidden][1]]
-# One chunk a thread: up to the rows whose CTAs an SM holds at once (148 SMs x 8 / 8 / 6 / 3 / 3).
-CASES += [(1184, 1032, 0), (1184, 1536, 1), (888, 2048, 0), (444, 3584, 0), (400, 3584, 1), (444, 4096, 0)]
+# One chunk a thread: up to the rows whose CTAs an SM holds at once (148 SMs x 8 / 8 / 6 / 3 / 3);
+# from H = 1536 with a weight off 16 bytes (the 256-bit stash kernel takes an aligned one).
+CASES += [(1184, 1032, 0), (1184, 1536, 1), (888, 2048, 1), (444, 3584, 1), (400, 3584, 1), (444, 4096, 1)]
 
 
 def _inputs(rows: int, hidden: int, seed: int):
@@ -73,8 +74,8 @@ def test_plain_few_rows(rows: int, hidden: int, w_off: int) -> None:
         g.assert_guards_intact()
 
 
-@pytest.mark.parametrize("rows, hidden", [(1, 3584), (7, 3584), (256, 4096), (33, 16384), (5, 1032), (296, 3584),
-                                         (592, 2048)])
+@pytest.mark.parametrize("rows, hidden", [(1, 3584), (7, 3584), (256, 4096), (33, 16384), (5, 1032), (296, 3576),
+                                         (592, 2040)])
 @torch.inference_mode()
 def test_fp8_few_rows(rows: int, hidden: int) -> None:
     x, r, w = _inputs(rows, hidden, rows + 7 * hidden)

@@ -40,6 +40,10 @@ def check(name: str, rows: int, hidden: int, x_off: int, o_off: int, w_off: int,
         phase = int(re.match(r"rmsnorm_shifted_kernel<(\d)", name).group(1))
         assert mode != "fp8" and x_off == o_off == phase and hidden % 8 == 0 and rows > 256, name
         assert hidden <= (12288 if mode == "fused" else 4096), name
+    elif kernel == "rmsnorm_stash_v8_kernel":
+        # 256-bit accesses: rows 32 bytes aligned, H % 16 == 0, a 16-byte aligned weight and fp8 output.
+        assert mode != "plain" and x_off == 0 and o_off == 0 and w_off == 0 and hidden % 16 == 0, name
+        assert 1536 <= hidden <= 5120 and 256 < rows <= 4096 and (mode != "fp8" or out8_off == 0), name
     elif kernel == "rmsnorm_cluster_kernel":
         assert aligned and 6144 <= hidden <= 131072, name
         if hidden <= 32768:
