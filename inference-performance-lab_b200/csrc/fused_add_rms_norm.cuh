@@ -1332,6 +1332,135 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_shifted_kernel(co
 }
 
 // ---------------------------------------------------------------------------------------------
+// The shifted kernel's scheme with 256-bit accesses (add+RMSNorm): rows that start kPhase
+// elements into a 32-byte block (x and residual alike), so that the H / 8 + 1 aligned 16-byte
+// chunks covering a row pair up into 32-byte blocks; H % 16 == 0, so the last pair holds only the
+// row's tail chunk, which is loaded and stored with 16 bytes (the chunk after it can lie past the
+// tensor's end). A thread owns one pair; its gamma is three aligned 16-byte loads (the chunk
+// before the pair and the pair's two), shifted by the phase, where two chunks took four. The
+// planner gives it a 16-byte aligned weight.
+template <int P>
+__device__ __forceinline__ U32x4 shift_window(const U32x4& lo, const U32x4& hi) {
+    const uint32_t win[8] = {lo.v[0], lo.v[1], lo.v[2], lo.v[3], hi.v[0], hi.v[1], hi.v[2], hi.v[3]};
+    constexpr int s = 8 - P;  // window element that is element 8a - P
+    constexpr uint32_t bits = 16u * static_cast<uint32_t>(s & 1);
+    U32x4 g;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) g.v[i] = __funnelshift_r(win[s / 2 + i], win[s / 2 + i + 1], bits);
+    return g;
+}
+
+constexpr int kShiftedV8MaxHidden = 4080;  // H / 16 + 1 pairs: at most 256 threads
+
+template <int kPhase>
+__global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_shifted_v8_kernel(const WarpRowParams p) {
+    __shared__ float partials[2][kStashMaxThreads / kWarpSize];
+    const int warps = static_cast<int>(blockDim.x) / kWarpSize;
+    const int q = threadIdx.x;                   // pair q: aligned chunks 2q and 2q + 1
+    const int last = p.hidden >> 4;              // the last pair: the tail chunk H / 8 alone
+    const bool active = q <= last;
+    const bool head = q == 0;
+    const bool tail = q == last;
+    const int warp = threadIdx.x / kWarpSize;
+    const int lane = threadIdx.x % kWarpSize;
+    const float hidden_f = static_cast<float>(p.hidden);
+    const U32x4 zero = {{0u, 0u, 0u, 0u}};
+
+    if (threadIdx.x == 0 && static_cast<int64_t>(blockIdx.x) < p.rows) {
+        const int64_t row = blockIdx.x;
+        const uint32_t bytes = 2u * static_cast<uint32_t>(p.hidden);
+        prefetch_span_l2(p.x + row * p.hidden, bytes);
+        prefetch_span_l2(p.residual + row * p.hidden, bytes);
+        if (blockIdx.x < kGammaPrefetchCtas) prefetch_span_l2(p.weight, bytes);
+    }
+    grid_dependency_wait();
+    grid_launch_dependents();
+    prefetch_next_wave_row<true>(p);
+
+    int parity = 0;
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        // Chunk c covers elements 8c - kPhase .. 8c - kPhase + 7 of the row; pair q starts at
+        // element 16q - kPhase, a 32-byte boundary.
+        uint16_t* xr = p.x + row * p.hidden - kPhase + 16 * q;
+        uint16_t* rr = p.residual + row * p.hidden - kPhase + 16 * q;
+        U32x4 x0 = zero, x1 = zero, r0 = zero, r1 = zero;
+        if (active) {
+            if (!tail) {
+                const U32x8 xs = ld_v8(xr), rs = ld_v8(rr);
+                x0 = {{xs.v[0], xs.v[1], xs.v[2], xs.v[3]}};
+                x1 = {{xs.v[4], xs.v[5], xs.v[6], xs.v[7]}};
+                r0 = {{rs.v[0], rs.v[1], rs.v[2], rs.v[3]}};
+                r1 = {{rs.v[4], rs.v[5], rs.v[6], rs.v[7]}};
+            } else {
+                x0 = ld_v4(xr);
+                r0 = ld_v4(rr);
+            }
+        }
+        F32x2 acc = f32x2_make(0.0f, 0.0f);
+        if (active) {
+            Pairs4 a = chunk_sum(x0, r0);
+            if (head) zero_span<0, kPhase>(a);
+            if (tail) zero_span<kPhase, 8>(a);
+            const U32x4 ra = chunk_to_bf16(a);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc = f32x2_fma(a.v[e], a.v[e], acc);
+            if (tail) {
+                store_span<0, kPhase>(rr, ra);
+            } else {
+                const Pairs4 b = chunk_sum(x1, r1);
+                const U32x4 rb = chunk_to_bf16(b);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc = f32x2_fma(b.v[e], b.v[e], acc);
+                if (head) {
+                    store_span<kPhase, 8>(rr, ra);
+                    st_v4(rr + 8, rb);
+                } else {
+                    st_v8(rr, {{ra.v[0], ra.v[1], ra.v[2], ra.v[3], rb.v[0], rb.v[1], rb.v[2], rb.v[3]}});
+                }
+            }
+        }
+        float acc_lo, acc_hi;
+        f32x2_split(acc, acc_lo, acc_hi);
+        const float warp_total = warp_sum(acc_lo + acc_hi);
+        if (lane == 0) partials[parity][warp] = warp_total;  // two parities: see rmsnorm_cta_kernel
+        __syncthreads();
+        float sumsq = 0.0f;
+        for (int w = 0; w < warps; ++w) sumsq += partials[parity][w];
+        parity ^= 1;
+        const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
+        const F32x2 inv2 = f32x2_make(inv, inv);
+        if (active) {
+            // Weight chunks 2q - 1, 2q and 2q + 1 (zero outside the weight); windows (2q - 1, 2q)
+            // and (2q, 2q + 1) are the pair's gamma.
+            const U32x4 wm = head ? zero : ld_shared_ro_v4(p.weight + 16 * q - 8);
+            const U32x4 w0 = tail ? zero : ld_shared_ro_v4(p.weight + 16 * q);
+            Pairs4 a = chunk_sum(x0, r0);
+            const Pairs4 ga = chunk_widen(shift_window<kPhase>(wm, w0));
+#pragma unroll
+            for (int e = 0; e < 4; ++e) a.v[e] = f32x2_mul(f32x2_mul(a.v[e], inv2), ga.v[e]);
+            const U32x4 oa = chunk_to_bf16(a);
+            uint16_t* orow = p.out + row * p.hidden - kPhase + 16 * q;
+            if (tail) {
+                store_span<0, kPhase>(orow, oa);
+            } else {
+                const U32x4 w1 = ld_shared_ro_v4(p.weight + 16 * q + 8);
+                Pairs4 b = chunk_sum(x1, r1);
+                const Pairs4 gb = chunk_widen(shift_window<kPhase>(w0, w1));
+#pragma unroll
+                for (int e = 0; e < 4; ++e) b.v[e] = f32x2_mul(f32x2_mul(b.v[e], inv2), gb.v[e]);
+                const U32x4 ob = chunk_to_bf16(b);
+                if (head) {
+                    store_span<kPhase, 8>(orow, oa);
+                    st_v4(orow + 8, ob);
+                } else {
+                    st_v8(orow, {{oa.v[0], oa.v[1], oa.v[2], oa.v[3], ob.v[0], ob.v[1], ob.v[2], ob.v[3]}});
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 
 __device__ __forceinline__ float block_sum_rowwise(float value, float* partials) {
     value = warp_sum(value);

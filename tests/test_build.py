@@ -81,6 +81,16 @@ def test_stash_v8_kernel_registers() -> None:
         assert regs <= 64 and spills == 0, (n, regs, spills)
 
 
+def test_shifted_v8_kernel_registers() -> None:
+    """The 256-bit shifted kernel's seven phase instances within 64 registers (four CTAs an SM)."""
+    res = kernel_resources()
+    names = [n for n in res if n.startswith("_ZN3ipl25rmsnorm_shifted_v8_kernel")]
+    assert len(names) == 7, names
+    for n in names:
+        regs, spills = res[n]
+        assert regs <= 64 and spills == 0, (n, regs, spills)
+
+
 def test_cluster_kernel_registers() -> None:
     """Nine instances (1, 2 and 4 chunks a thread; three modes), each within the 64 registers that
     let two CTAs of 512 threads, or four of 256, share an SM."""

@@ -230,9 +230,17 @@ def test_rms_plan_selection() -> None:
     assert rms_plan(0, 0, 0, 2048, 3584) == "rmsnorm_stash_v8_kernel"
     assert rms_plan(0, 0, 1, 2048, 3584) == "rmsnorm_stash_kernel<4>"
     # x and residual both off 16 bytes alike, more than 256 rows: the shifted kernel, one instance
-    # per phase, up to H = 12288; fewer rows or longer ones: the staged kernel.
+    # per phase, up to H = 12288; fewer rows or longer ones: the staged kernel. 257-4096 rows of
+    # 1536-4080 elements (H % 16 == 0) with a 16-byte aligned weight, rows in the first half of a
+    # 32-byte block: its 256-bit variant.
     for off in range(1, 8):
-        assert rms_plan(off, off, 0, 2048, 3584) == f"rmsnorm_shifted_kernel<{off}>"
+        assert rms_plan(off, off, 0, 2048, 3584) == f"rmsnorm_shifted_v8_kernel<{off}>"
+        assert rms_plan(off, off, 1, 2048, 3584) == f"rmsnorm_shifted_kernel<{off}>"
+        assert rms_plan(off + 8, off + 8, 0, 2048, 3584) == f"rmsnorm_shifted_kernel<{off}>"  # second half
+    assert rms_plan(1, 1, 0, 4097, 3584) == "rmsnorm_shifted_kernel<1>"
+    assert rms_plan(1, 1, 0, 2048, 4096) == "rmsnorm_shifted_kernel<1>"
+    assert rms_plan(1, 1, 0, 2048, 4080) == "rmsnorm_shifted_v8_kernel<1>"
+    assert capi.rms_norm_plan(BASE + 2, BASE + (1 << 34) + 2, BASE + 8192, 2048, 3584) == "rmsnorm_shifted_kernel<1, plain>"
     assert rms_plan(3, 3, 1, 300, 12288) == "rmsnorm_shifted_kernel<3>"
     assert rms_plan(1, 1, 0, 256, 3584).startswith("rmsnorm_staged_kernel")
     assert rms_plan(1, 1, 0, 2048, 12296).startswith("rmsnorm_staged_kernel")

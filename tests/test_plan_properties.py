@@ -36,6 +36,10 @@ def check(name: str, rows: int, hidden: int, x_off: int, o_off: int, w_off: int,
         assert hidden <= limit, name
         if kernel == "rmsnorm_cta_kernel" and rows > 256:
             assert hidden <= 4096, name  # above 256 rows only one chunk a thread, one wave
+    elif kernel == "rmsnorm_shifted_v8_kernel":
+        phase = int(re.match(r"rmsnorm_shifted_v8_kernel<(\d)", name).group(1))
+        assert mode == "fused" and x_off == o_off == phase and w_off == 0 and hidden % 16 == 0, name
+        assert 1536 <= hidden <= 4080 and 256 < rows <= 4096, name
     elif kernel == "rmsnorm_shifted_kernel":
         phase = int(re.match(r"rmsnorm_shifted_kernel<(\d)", name).group(1))
         assert mode != "fp8" and x_off == o_off == phase and hidden % 8 == 0 and rows > 256, name

@@ -176,7 +176,10 @@ def test_fused_shifted_rows(rows: int, hidden: int, off: int, w_off: int) -> Non
     gx, gr, gw = Guarded(x.shape, off), Guarded(x.shape, off), Guarded(w.shape, w_off)
     ax, ar, aw = gx.load(oracle.tensor_bits(x)), gr.load(oracle.tensor_bits(r)), gw.load(oracle.tensor_bits(w))
     plan = capi.fused_add_rms_norm_plan(ax.data_ptr(), ar.data_ptr(), aw.data_ptr(), rows, hidden)
-    assert plan == f"rmsnorm_shifted_kernel<{off}>", plan
+    # With a 16-byte aligned weight, rows of 1536-4080 elements (H % 16 == 0) go to the 256-bit
+    # variant (tests/test_shifted_v8_rows.py).
+    v8 = w_off == 0 and hidden % 16 == 0 and 1536 <= hidden <= 4080 and rows <= 4096
+    assert plan == (f"rmsnorm_shifted_v8_kernel<{off}>" if v8 else f"rmsnorm_shifted_kernel<{off}>"), plan
     torch.ops.inference_performance_lab.fused_add_rms_norm(ax, ar, aw, 1e-6)
     out, res = oracle.c_fused_add_rms_norm(oracle.tensor_bits(x), oracle.tensor_bits(r), oracle.tensor_bits(w), 1e-6)
     assert_bits_equal(ar, res, f"{rows}x{hidden}+{off} residual")
@@ -209,7 +212,7 @@ def test_shifted_graph_replay_matches_eager() -> None:
     gx, gr = Guarded(x.shape, off), Guarded(x.shape, off)
     ex, er = gx.load(oracle.tensor_bits(x)), gr.load(oracle.tensor_bits(r))
     assert capi.fused_add_rms_norm_plan(ex.data_ptr(), er.data_ptr(), w.data_ptr(), rows, hidden) == (
-        "rmsnorm_shifted_kernel<3>"
+        "rmsnorm_shifted_v8_kernel<3>"
     )
     for _ in range(2):
         torch.ops.inference_performance_lab.fused_add_rms_norm(ex, er, w, 1e-6)
