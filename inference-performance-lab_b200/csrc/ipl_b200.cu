@@ -756,11 +756,12 @@ ipl_status run_rms(uint16_t* x, uint16_t* residual, uint16_t* out, uint8_t* out8
 // ------------------------------------------------------------------------------------------
 // SiLU-and-mul planning
 
-enum class SiluKernel { kNone, kVector32, kVector16, kScalar };
+enum class SiluKernel { kNone, kWave16, kVector32, kVector16, kScalar };
 
 const char* silu_kernel_name(SiluKernel k) {
     switch (k) {
         case SiluKernel::kNone: return "none";
+        case SiluKernel::kWave16: return "silu_wave_kernel";
         case SiluKernel::kVector32: return "silu_vector_kernel<32>";
         case SiluKernel::kVector16: return "silu_vector_kernel<16>";
         case SiluKernel::kScalar: return "silu_scalar_kernel";
@@ -782,11 +783,15 @@ ipl_status check_silu_args(const void* output, const void* input, int64_t rows, 
     return IPL_SUCCESS;
 }
 
-SiluKernel plan_silu(const void* output, const void* input, int64_t rows, int64_t inter) {
+SiluKernel plan_silu(const void* output, const void* input, int64_t rows, int64_t inter, int sm_count) {
     if (rows * inter == 0) return SiluKernel::kNone;
     const uintptr_t a = reinterpret_cast<uintptr_t>(output) | reinterpret_cast<uintptr_t>(input);
     const uint64_t packs32 = static_cast<uint64_t>(rows) * static_cast<uint64_t>(inter / 16);
     const uint64_t packs16 = static_cast<uint64_t>(rows) * static_cast<uint64_t>(inter / 8);
+    // One 16-byte pack per thread in a single wave of two 1024-thread CTAs per SM, when the packs
+    // fill more than one such CTA per SM.
+    const uint64_t wave16 = static_cast<uint64_t>(sm_count) * 2 * kSiluWaveThreads;
+    if (inter % 8 == 0 && (a & 15u) == 0 && packs16 > wave16 / 2 && packs16 <= wave16) return SiluKernel::kWave16;
     if (inter % 16 == 0 && (a & 31u) == 0 && packs32 <= UINT32_MAX) return SiluKernel::kVector32;
     if (inter % 8 == 0 && (a & 15u) == 0 && packs16 <= UINT32_MAX) return SiluKernel::kVector16;
     return SiluKernel::kScalar;
@@ -839,7 +844,19 @@ ipl_status run_silu(void* output, const void* input, int64_t rows, int64_t inter
     auto* out = static_cast<uint16_t*>(output);
     const auto* in = static_cast<const uint16_t*>(input);
     cudaError_t err = cudaSuccess;
-    switch (plan_silu(output, input, rows, inter)) {
+    switch (plan_silu(output, input, rows, inter, sms)) {
+        case SiluKernel::kWave16: {
+            SiluVectorParams p;
+            p.out = out;
+            p.in = in;
+            p.intermediate = inter;
+            const uint32_t per_row = static_cast<uint32_t>(inter / 8);
+            p.total_packs = static_cast<uint32_t>(rows) * per_row;
+            p.packs_per_row = make_fast_div32(per_row);
+            const unsigned grid = (p.total_packs + kSiluWaveThreads - 1) / kSiluWaveThreads;
+            err = launch(silu_wave_kernel, grid, kSiluWaveThreads, 0, stream, p);
+            break;
+        }
         case SiluKernel::kVector32:
             err = launch_silu_vector<32>(out, in, rows, inter, sms, stream);
             break;
@@ -990,7 +1007,9 @@ const char* ipl_fused_add_rms_norm_static_fp8_quant_plan(const void* output, con
 const char* ipl_silu_and_mul_plan(const void* output, const void* input, int64_t rows,
                                   int64_t intermediate_size) {
     if (check_silu_args(output, input, rows, intermediate_size) != IPL_SUCCESS) return "invalid";
-    return silu_kernel_name(plan_silu(output, input, rows, intermediate_size));
+    int sms = 0, smem = 0;
+    plan_limits(&sms, &smem);
+    return silu_kernel_name(plan_silu(output, input, rows, intermediate_size, sms));
 }
 
 }  // extern "C"

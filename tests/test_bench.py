@@ -86,7 +86,7 @@ def test_our_arm_prints_the_full_contract_line_on_a_gpu() -> None:
     assert d["parity"]["parity_ok"] and d["parity"]["residual_exact"] and d["parity"]["rows_checked"] == 2048
     # The other three workloads, measured in the same run and checked against the oracle.
     for key, kernel_prefix in (("sharded", "rmsnorm_stash_kernel"), ("misaligned", "rmsnorm_shifted_"),
-                               ("silu", "silu_vector_kernel")):
+                               ("silu", "silu_wave_kernel")):
         sub = d[key]
         assert sub["kernel"].startswith(kernel_prefix), (key, sub["kernel"])
         assert sub["parity"]["parity_ok"] and sub["parity"]["parity_ok_all_ranks"], (key, sub["parity"])

@@ -102,6 +102,16 @@ def test_cluster_kernel_registers() -> None:
         assert regs <= 64 and spills == 0, (n, regs, spills)
 
 
+def test_silu_wave_kernel_registers() -> None:
+    """The one-wave SiLU kernel within the 32 registers that let two CTAs of 1024 threads share an
+    SM (2 x 1024 x 32 = 65,536)."""
+    res = kernel_resources()
+    names = [n for n in res if n.startswith("_ZN3ipl16silu_wave_kernel")]
+    assert len(names) == 1, names
+    regs, spills = res[names[0]]
+    assert regs <= 32 and spills == 0, (names[0], regs, spills)
+
+
 def test_no_kernel_spills() -> None:
     res = kernel_resources()
     spilling = {n: s for n, (_, s) in res.items() if s}

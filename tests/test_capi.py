@@ -81,7 +81,7 @@ def test_c_caller_builds_links_and_runs(tmp_path: Path) -> None:
                    check=True, capture_output=True, text=True)
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines()
     assert out[0] == "rmsnorm_stash_v8_kernel"
-    assert out[1] == "silu_vector_kernel<32>"
+    assert out[1] == "silu_wave_kernel"
     assert out[2] == "IPL_ERROR_INVALID_VALUE: epsilon must be positive"
     assert out[3].startswith("IPL_ERROR_MISALIGNED: ") and "divisible by 8" in out[3]
 
@@ -382,9 +382,18 @@ def test_cluster_plan_selection() -> None:
 
 
 def test_silu_plan_selection() -> None:
-    assert silu_plan(0, 0, 128, 18944) == "silu_vector_kernel<32>"
-    assert silu_plan(8, 0, 128, 18944) == "silu_vector_kernel<16>"
-    assert silu_plan(0, 0, 128, 18952) == "silu_vector_kernel<16>"
+    # 128 x 2368 = 303,104 16-byte packs: one wave of 148 SMs x 2048 threads, one pack a thread.
+    assert silu_plan(0, 0, 128, 18944) == "silu_wave_kernel"
+    assert silu_plan(8, 0, 128, 18944) == "silu_wave_kernel"
+    assert silu_plan(0, 0, 127, 18952) == "silu_wave_kernel"
+    assert silu_plan(0, 0, 128, 18952) == "silu_vector_kernel<16>"  # 303,232 packs: above one wave
+    # At most half a wave, or more than one: one 32-byte pack a thread where aligned, else 16.
+    assert silu_plan(0, 0, 64, 18944) == "silu_vector_kernel<32>"
+    assert silu_plan(0, 0, 65, 18944) == "silu_wave_kernel"
+    assert silu_plan(0, 0, 129, 18944) == "silu_vector_kernel<32>"
+    assert silu_plan(8, 0, 2048, 18944) == "silu_vector_kernel<16>"
+    assert silu_plan(0, 0, 2048, 18952) == "silu_vector_kernel<16>"
+    assert silu_plan(4, 0, 128, 18944) == "silu_scalar_kernel"  # 8 bytes off: no 16-byte packs
     assert silu_plan(0, 0, 3, 1001) == "silu_scalar_kernel"
     assert silu_plan(1, 0, 128, 18944) == "silu_scalar_kernel"
     assert silu_plan(0, 0, 0, 18944) == "none"

@@ -92,7 +92,10 @@ def test_silu_plans_take_the_widest_vector_their_alignment_allows(rows, inter, o
         assert name == "none"
         return
     offset_bytes = (2 * out_off) | (2 * in_off)
-    if inter % 16 == 0 and offset_bytes % 32 == 0:
+    packs16 = rows * (inter // 8)
+    if inter % 8 == 0 and offset_bytes % 16 == 0 and 148 * 1024 < packs16 <= 148 * 2048:
+        assert name == "silu_wave_kernel", name  # one 16-byte pack a thread, one wave of 148 x 2048 threads
+    elif inter % 16 == 0 and offset_bytes % 32 == 0:
         assert name == "silu_vector_kernel<32>", name  # 32-byte packs: gate, up and out rows all aligned
     elif inter % 8 == 0 and offset_bytes % 16 == 0:
         assert name == "silu_vector_kernel<16>", name
