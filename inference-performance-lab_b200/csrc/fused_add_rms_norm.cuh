@@ -956,8 +956,6 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_stash_v8_kernel(c
         cp_async_16(gamma_base, p.weight + 16 * q);
         cp_async_16(gamma_base + 16u, p.weight + 16 * q + 8);
     }
-    const float scale_inv = kFp8 ? 1.0f / *p.scale : 1.0f;
-    const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
 
     int parity = 0;
     for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
@@ -984,6 +982,11 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_stash_v8_kernel(c
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc = f32x2_fma(b.v[e], b.v[e], acc);
         }
+        // The fp8 op's scale, read behind the row's loads and inverted after the barrier: read
+        // ahead of them, its round trip held up every CTA's loads (fp8 output at [2048, 3584] on
+        // B200: 9.33 against 9.07 us a launch over 3000 steps, the same bits).
+        float scale = 1.0f;
+        if constexpr (kFp8) scale = ld_nc_f32(p.scale);
         float acc_lo, acc_hi;
         f32x2_split(acc, acc_lo, acc_hi);
         const float warp_total = warp_sum(acc_lo + acc_hi);
@@ -995,6 +998,8 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_stash_v8_kernel(c
         parity ^= 1;
         const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
         const F32x2 inv2 = f32x2_make(inv, inv);
+        const float scale_inv = kFp8 ? 1.0f / scale : 1.0f;
+        const F32x2 scale_inv2 = f32x2_make(scale_inv, scale_inv);
         if (active) {
             const U32x4 x0 = {{xs.v[0], xs.v[1], xs.v[2], xs.v[3]}}, x1 = {{xs.v[4], xs.v[5], xs.v[6], xs.v[7]}};
             Pairs4 a, b;
@@ -1338,6 +1343,10 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_shifted_kernel(co
 // row's tail chunk, which is loaded and stored with 16 bytes (the chunk after it can lie past the
 // tensor's end). A thread owns one pair; its gamma is three aligned 16-byte loads (the chunk
 // before the pair and the pair's two), shifted by the phase, where two chunks took four. The
+// gamma loads are issued right behind the row's loads and shifted before the reduction, so that
+// pass 2 starts from registers after the barrier: measured on B200 (chained launches at
+// [2048, 3584], phase 1, the same bits) 10.16 against 10.62 us a launch with the loads after the
+// barrier; gamma staged in shared memory by cp.async instead was level with the latter. The
 // planner gives it a 16-byte aligned weight.
 template <int P>
 __device__ __forceinline__ U32x4 shift_window(const U32x4& lo, const U32x4& hi) {
@@ -1396,6 +1405,16 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_shifted_v8_kernel
                 r0 = ld_v4(rr);
             }
         }
+        // Weight chunks 2q - 1, 2q and 2q + 1 (zero outside the weight); windows (2q - 1, 2q) and
+        // (2q, 2q + 1) are the pair's gamma.
+        U32x4 gamma_a = zero, gamma_b = zero;
+        if (active) {
+            const U32x4 wm = head ? zero : ld_shared_ro_v4(p.weight + 16 * q - 8);
+            const U32x4 w0 = tail ? zero : ld_shared_ro_v4(p.weight + 16 * q);
+            const U32x4 w1 = tail ? zero : ld_shared_ro_v4(p.weight + 16 * q + 8);
+            gamma_a = shift_window<kPhase>(wm, w0);
+            gamma_b = shift_window<kPhase>(w0, w1);
+        }
         F32x2 acc = f32x2_make(0.0f, 0.0f);
         if (active) {
             Pairs4 a = chunk_sum(x0, r0);
@@ -1430,12 +1449,8 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_shifted_v8_kernel
         const float inv = 1.0f / sqrtf(__fdiv_rn(sumsq, hidden_f) + p.epsilon);
         const F32x2 inv2 = f32x2_make(inv, inv);
         if (active) {
-            // Weight chunks 2q - 1, 2q and 2q + 1 (zero outside the weight); windows (2q - 1, 2q)
-            // and (2q, 2q + 1) are the pair's gamma.
-            const U32x4 wm = head ? zero : ld_shared_ro_v4(p.weight + 16 * q - 8);
-            const U32x4 w0 = tail ? zero : ld_shared_ro_v4(p.weight + 16 * q);
             Pairs4 a = chunk_sum(x0, r0);
-            const Pairs4 ga = chunk_widen(shift_window<kPhase>(wm, w0));
+            const Pairs4 ga = chunk_widen(gamma_a);
 #pragma unroll
             for (int e = 0; e < 4; ++e) a.v[e] = f32x2_mul(f32x2_mul(a.v[e], inv2), ga.v[e]);
             const U32x4 oa = chunk_to_bf16(a);
@@ -1443,9 +1458,8 @@ __global__ void __launch_bounds__(kStashMaxThreads, 2) rmsnorm_shifted_v8_kernel
             if (tail) {
                 store_span<0, kPhase>(orow, oa);
             } else {
-                const U32x4 w1 = ld_shared_ro_v4(p.weight + 16 * q + 8);
                 Pairs4 b = chunk_sum(x1, r1);
-                const Pairs4 gb = chunk_widen(shift_window<kPhase>(w0, w1));
+                const Pairs4 gb = chunk_widen(gamma_b);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) b.v[e] = f32x2_mul(f32x2_mul(b.v[e], inv2), gb.v[e]);
                 const U32x4 ob = chunk_to_bf16(b);

@@ -150,6 +150,12 @@ __device__ __forceinline__ U32x8 ld_v8(const void* p) {
                  : "l"(p));
     return r;
 }
+// Read-only 4-byte load, ordered after the volatile loads issued before it in program order.
+__device__ __forceinline__ float ld_nc_f32(const float* p) {
+    float r;
+    asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(r) : "l"(p));
+    return r;
+}
 // Read-only 16-byte load that may stay in L1 (data every CTA on the SM reads, e.g. gamma).
 __device__ __forceinline__ U32x4 ld_shared_ro_v4(const void* p) {
     U32x4 r;
